@@ -1,0 +1,449 @@
+"""Benchmark of the paged-decode hot path (and fused add + RMSNorm) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}] [--workload ...]
+
+For N > 1 launch one process per GPU:
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N
+
+Workload (default ``decode``): kernel-lab's headline, paged decode attention with Llama-3-8B
+heads (32 query / 8 KV, head_dim 128, 16-token pages), bf16, batch 64, context 4096,
+shuffled pages, NaN-poisoned spare pages. A step is one decode call. At N GPUs the KV
+heads are sharded N ways (tensor parallel) and the batch grows to 64*N, so every GPU
+streams the same 1.07 GB of KV per step (weak scaling); the per-head outputs are
+all-gathered with NCCL inside the step. ``decode70b``: Llama-3-70B heads (64/8), batch
+256, context 8192, total work fixed across N (strong scaling). ``rmsnorm``: fused add +
+RMSNorm, 4096 x 8192 bf16.
+
+One JSON line on rank 0: value = aggregate algorithmic HBM GB/s (K+V read once, q and
+out once: kernel-lab's byte model) over the max-over-ranks device time; ``roofline`` for
+the decode kernel (its own CUDA-event time); ``e2e`` through the torch op with pinned host
+inputs copied in and the output copied out every step; ``cpu_baseline`` = the oracle
+(NumPy restatement of kernel-lab's PyTorch CPU reference) on this host's cores.
+``--impl reference`` times that CPU path alone (kernel-lab's own implementation of the
+path is PyTorch-on-CPU; its restatement stands in for it on the GPU box).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path[:0] = [str(REPO), str(REPO / "kernel-lab_b200")]
+
+METRIC = "paged decode attn % of B200 peak HBM BW (Llama-3-8B GQA bs64 ctx4096); us/call"
+RMS_METRIC = "fused add+RMSNorm % of B200 peak HBM BW (4096 tokens x 8192 hidden, bf16); us/call"
+L2_NOTE = "inputs larger than L2 (no flush needed)"
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "ours", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["decode", "decode70b", "rmsnorm"], default="decode")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def workload_spec(name: str, world: int) -> dict:
+    if name == "decode":
+        return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
+                    desc="paged decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU, ctx 4096")
+    if name == "decode70b":
+        return dict(kind="decode", batch=256, ctx=8192, hq=64, hkv=8, d=128, page=16, scaling="strong",
+                    desc="paged decode, Llama-3-70B heads 64/8/128, page 16, bf16, batch 256, ctx 8192")
+    return dict(kind="rmsnorm", rows=4096, hidden=8192, scaling="weak",
+                desc="fused residual-add + RMSNorm, 4096 x 8192 bf16, eps 1e-5")
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, clock-event reasons) every few ms on a side thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: report no clocks
+            self._nvml = None
+
+    def _sample(self):
+        n = self._nvml
+        mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+        reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        self.samples.append((mhz, reasons))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self._nvml:
+            self._sample()
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._nvml:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+
+    def summary(self) -> dict | None:
+        if not self._nvml or not self.samples:
+            return None
+        reasons = 0
+        for _, r in self.samples:
+            reasons |= r
+        names = sorted(k for k, bit in self.REASONS.items() if reasons & bit and k != "gpu_idle")
+        return {
+            "sm_mhz": statistics.median(m for m, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": names,
+            "samples": len(self.samples),
+        }
+
+
+# ----------------------------------------------------------------------------- CPU side
+
+
+def cpu_measure(kind: str, spec: dict, seconds: float, dtype: str = "bf16", warmup: int = 1) -> dict:
+    """The oracle on this host: whole sample units per step, until `seconds` of timed work."""
+    from oracle.oracle import decode_bytes
+    from oracle.timing import CpuOracleRunner
+
+    if kind == "decode":
+        unit = dict(ctx=spec["ctx"], hq=spec["hq"] // spec.get("tp", 1), hkv=spec["hkv"] // spec.get("tp", 1),
+                    d=spec["d"], page=spec["page"], dtype=dtype)
+        unit_bytes = decode_bytes([unit["ctx"]], unit["hq"], unit["hkv"], unit["d"], 2)
+        what = f"sequences of ctx {unit['ctx']} with {unit['hq']}/{unit['hkv']}/{unit['d']} heads"
+    else:
+        unit = dict(rows=64, hidden=spec["hidden"], dtype=dtype)
+        unit_bytes = 4 * 64 * spec["hidden"] * 2 + spec["hidden"] * 2
+        what = f"blocks of 64 rows x {spec['hidden']}"
+    with CpuOracleRunner(kind, unit) as runner:
+        for _ in range(warmup):
+            runner.step()
+        times = []
+        while sum(times) < seconds or len(times) < 2:
+            times.append(runner.step())
+        workers = runner.workers
+    units = workers * len(times)
+    total = sum(times)
+    return {
+        "value": units * unit_bytes / total / 1e9,
+        "unit": "GB/s",
+        "cores": workers,
+        "kind": "port",
+        "sample": f"{units} {what} ({workers} processes x {len(times)} steps, {total:.1f} s), NumPy oracle",
+        "seconds_per_step": total / len(times),
+        "units_per_step": workers,
+        "unit_bytes": unit_bytes,
+    }
+
+
+def run_reference(args, spec: dict) -> None:
+    """Reference arm: kernel-lab's CPU path (its NumPy restatement) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    kind = spec["kind"]
+    from oracle.timing import CpuOracleRunner
+
+    if kind == "decode":
+        unit = dict(ctx=spec["ctx"], hq=spec["hq"], hkv=spec["hkv"], d=spec["d"], page=spec["page"], dtype="bf16")
+        from oracle.oracle import decode_bytes
+
+        unit_bytes = decode_bytes([spec["ctx"]], spec["hq"], spec["hkv"], spec["d"], 2)
+    else:
+        unit = dict(rows=64, hidden=spec["hidden"], dtype="bf16")
+        unit_bytes = 4 * 64 * spec["hidden"] * 2 + spec["hidden"] * 2
+    with CpuOracleRunner(kind, unit) as runner:
+        for _ in range(args.warmup):
+            runner.step()
+        times = [runner.step() for _ in range(args.steps)]
+        workers = runner.workers
+    total = sum(times)
+    value = workers * len(times) * unit_bytes / total / 1e9
+    line = {
+        "metric": METRIC if kind == "decode" else RMS_METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total / len(times) * 1e3,
+        "higher_is_better": True,
+        "scaling": spec["scaling"],
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), bf16-rounded)",
+        "impl": "reference",
+        "config": {"workload": spec["desc"], "sample_per_step": f"{workers} units of the workload"},
+        "cpu_baseline": {
+            "value": value,
+            "unit": "GB/s",
+            "cores": workers,
+            "kind": "port",
+            "sample": f"each step: {workers} sequences/blocks of the workload, one per process",
+        },
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU side
+
+
+def load_traffic(key: str) -> float | None:
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    try:
+        return json.loads((REPO / "profiles" / "traffic.json").read_text())[key]["bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def main() -> None:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    spec = workload_spec(args.workload, world)
+    if args.impl == "reference":
+        run_reference(args, spec)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from kernel_lab import cuda_ops
+    from kernel_lab.roofline import B200_SPEC_HBM_GBPS, decode_attention_work, measured_peaks, rms_norm_work
+
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    if not cuda_ops.available():
+        raise SystemExit(f"kernel_lab CUDA path unavailable: {cuda_ops.why_unavailable()}")
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    peaks = measured_peaks()
+
+    if spec["kind"] == "decode":
+        from kernel_lab.kv_cache import random_paged_pool
+        from kernel_lab.sharding import gather_heads, kv_head_range
+
+        B, ctx, hq, hkv, d, page = (spec[k] for k in ("batch", "ctx", "hq", "hkv", "d", "page"))
+        lo, hi = kv_head_range(hkv, world, rank)
+        q, kv = random_paged_pool([ctx] * B, hq, hkv, d, page, dtype=torch.bfloat16, device=dev, seed=1234,
+                                  kv_head_slice=(lo, hi))
+        hq_l, hkv_l = q.shape[1], hi - lo
+        scale = d**-0.5
+        out_local = torch.empty_like(q)
+        out_full = torch.empty((B, hq, d), dtype=q.dtype, device=dev)
+        kernel_work = decode_attention_work([ctx] * B, hq_l, hkv_l, d, 2)  # per rank, per launch
+        job_bytes = decode_attention_work([ctx] * B, hq, hkv, d, 2).bytes
+
+        def kernel():
+            torch.ops.kernel_lab.paged_decode_attention(out_local, q, kv.k_cache, kv.v_cache, kv.block_table,
+                                                        kv.seq_lens, scale)
+
+        def step():
+            kernel()
+            if world > 1:
+                gather_heads(out_local, world, out=out_full)
+
+        metric = METRIC
+    else:
+        R, H = spec["rows"], spec["hidden"]
+        g = torch.Generator(device=dev).manual_seed(7)
+        x = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+        res = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+        w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        kernel_work = rms_norm_work(R, H, 2, True)
+        job_bytes = kernel_work.bytes * world
+
+        def kernel():
+            torch.ops.kernel_lab.fused_add_rms_norm(out, x, res, w, 1e-5)
+
+        step = kernel
+        metric = RMS_METRIC
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---- timed region: exactly K steps, CUDA events on the launching stream
+    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(args.steps):
+            k_start[i].record(stream)
+            kernel()
+            k_end[i].record(stream)
+            if world > 1 and spec["kind"] == "decode":
+                gather_heads(out_local, world, out=out_full)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    step_ms = t0.elapsed_time(t1) / args.steps
+    kern_ms = sum(a.elapsed_time(b) for a, b in zip(k_start, k_end, strict=True)) / args.steps
+    tt = torch.tensor([step_ms, kern_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms = tt.tolist()
+
+    # ---- end to end through the torch op: pinned host inputs in, result out, every step
+    e2e = None
+    if spec["kind"] == "decode":
+        q_h = q.cpu().pin_memory()
+        bt_h = kv.block_table.cpu().pin_memory()
+        ln_h = kv.seq_lens.cpu().pin_memory()
+        out_h = torch.empty(out_full.shape if world > 1 else out_local.shape, dtype=q.dtype).pin_memory()
+        h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + ln_h.numel() * 4
+        d2h = out_h.numel() * out_h.element_size()
+
+        def e2e_step():
+            q.copy_(q_h, non_blocking=True)
+            kv.block_table.copy_(bt_h, non_blocking=True)
+            kv.seq_lens.copy_(ln_h, non_blocking=True)
+            torch.ops.kernel_lab.paged_decode_attention(out_local, q, kv.k_cache, kv.v_cache, kv.block_table,
+                                                        kv.seq_lens, scale)
+            src = out_local
+            if world > 1:
+                src = gather_heads(out_local, world, out=out_full)
+            out_h.copy_(src, non_blocking=True)
+    else:
+        x_h = x.cpu().pin_memory()
+        res_h = res.cpu().pin_memory()
+        out_h = torch.empty_like(x_h).pin_memory()
+        res_back = torch.empty_like(x_h).pin_memory()
+        h2d = 2 * x_h.numel() * 2
+        d2h = 2 * out_h.numel() * 2
+
+        def e2e_step():
+            x.copy_(x_h, non_blocking=True)
+            res.copy_(res_h, non_blocking=True)
+            torch.ops.kernel_lab.fused_add_rms_norm(out, x, res, w, 1e-5)
+            out_h.copy_(out, non_blocking=True)
+            res_back.copy_(res, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(10, min(args.steps, 100))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = te.item()
+    e2e = {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d * world),
+           "d2h_bytes_per_step": int(d2h * (1 if spec["kind"] == "decode" else world)), "ms_per_step": e2e_ms}
+
+    status = cuda_ops.decode_status(clear=True) if spec["kind"] == "decode" else 0
+
+    if rank == 0:
+        achieved = kernel_work.bytes / (kern_ms * 1e-3) / 1e9
+        key = f"{args.workload}_n{world}"
+        traffic = load_traffic(key)
+        value = job_bytes / (step_ms * 1e-3) / 1e9
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_measure(spec["kind"], spec, args.cpu_seconds)
+        cfg = {"workload": spec["desc"], "l2": L2_NOTE, "parallelism": f"kv-head tp{world}" if world > 1 else "1 gpu"}
+        if spec["kind"] == "decode":
+            cfg.update(batch=spec["batch"], ctx=spec["ctx"], num_q_heads=spec["hq"], num_kv_heads=spec["hkv"],
+                       head_dim=spec["d"], page_size=spec["page"], pool_pages=int(kv.k_cache.shape[0]),
+                       kv_bytes_per_gpu=int(kernel_work.bytes), planner="load-balanced (num_splits=0)")
+        else:
+            cfg.update(rows=spec["rows"], hidden=spec["hidden"], eps=1e-5)
+        line = {
+            "metric": metric,
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": step_ms,
+            "us_per_call": kern_ms * 1e3,
+            "pct_of_spec_peak_hbm": 100 * achieved / B200_SPEC_HBM_GBPS,
+            "higher_is_better": True,
+            "scaling": spec["scaling"],
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/K/V, shuffled pages, NaN spare pages)" if spec["kind"] == "decode"
+            else "synthetic (seeded x, residual ~ N(0,1), weight ~ N(1, 0.1))",
+            "impl": "b200",
+            "config": cfg,
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peaks.hbm_gbps,
+                "unit": "GB/s",
+                "frac": achieved / peaks.hbm_gbps,
+                "peak_source": f"{peaks.source} (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+                if peaks.source == "measured" else "fallback 6650 GB/s",
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": int(kernel_work.bytes),
+                "kernel": "decode_tc_kernel" if spec["kind"] == "decode" else "rmsnorm_row_regs",
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps,
+            "status_bits": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+/*
+ * kernel_lab_b200.h -- C ABI of the B200 (sm_100a) kernels for kernel-lab's two hot paths:
+ * fused residual-add + RMSNorm, and paged-KV single-token decode attention.
+ *
+ * Shared library: libkernel_lab_b200.so. Plain C types only: device pointers are
+ * `void*`, a stream is a `cudaStream_t` passed as `void*` (NULL = legacy default
+ * stream). Every entry point returns 0 on success or a `cudaError_t` code (as int);
+ * nothing throws across the ABI. Work is enqueued on the given stream; no call
+ * synchronises the host except kl_paged_decode_read_status.
+ *
+ * Layouts (all row-major, contiguous unless a stride is given):
+ *   x, residual, out   [rows, hidden]   (x rows are x_row_stride elements apart)
+ *   weight             [hidden]
+ *   q, out             [batch, num_q_heads, head_dim]
+ *   k_cache, v_cache   [num_pages, page_size, num_kv_heads, head_dim]        ("NHD")
+ *   block_table        [batch, >= max_pages_per_seq] int32, rows block_table_stride apart
+ *   seq_lens           [batch] int32
+ * Query head h attends with KV head h / (num_q_heads / num_kv_heads) (GQA / MQA).
+ */
+#ifndef KERNEL_LAB_B200_H_
+#define KERNEL_LAB_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Storage dtypes; same order as kernel_lab::DType (csrc/kernel_lab.h:12 in kernel-lab). */
+enum {
+  KL_FLOAT32 = 0,
+  KL_FLOAT16 = 1,
+  KL_BFLOAT16 = 2
+};
+
+/* Status bits a decode call leaves in word 0 of its sync buffer (sticky; see
+ * kl_paged_decode_read_status). */
+enum {
+  KL_STATUS_BAD_PAGE = 1,     /* a block-table entry outside [0, num_pages): that page was skipped */
+  KL_STATUS_LEN_CLAMPED = 2,  /* a sequence longer than max_pages_per_seq * page_size was clamped */
+  KL_STATUS_WAIT_TIMEOUT = 4  /* an internal pipeline wait exceeded its time limit; output is invalid */
+};
+
+/* Library version string, e.g. "kernel_lab_b200 0.1.0 sm_100a". */
+const char* kl_version(void);
+
+/* Human-readable text for a status code returned by any kl_* call. */
+const char* kl_status_string(int status);
+
+/*
+ * RMSNorm over rows of length `hidden`. With `residual` non-NULL this is the fused
+ * pre-norm step: residual <- dtype(x + residual) (in place, bit-exact), then
+ * out <- dtype(residual * rsqrt(mean(residual^2) + eps) * weight). With `residual`
+ * NULL: out <- rmsnorm(x). fp32 math. rows == 0 is a no-op.
+ *
+ * Replaces kernel_lab::launch_rms_norm (csrc/kernel_lab.h:14-19 in kernel-lab), same
+ * arguments; called by the torch ops rms_norm / fused_add_rms_norm
+ * (csrc/torch_bindings.cpp:31-69).
+ */
+int kl_rms_norm(int dtype, void* out, const void* x, void* residual, const void* weight, int rows,
+                int hidden, int64_t x_row_stride, float eps, void* stream);
+
+/*
+ * Scratch needed by kl_paged_decode for this problem on the current device:
+ *   *partial_bytes: per-split partial outputs (no initialisation needed);
+ *   *sync_bytes:    status word + one arrival counter per (sequence, KV head); must
+ *                   be zero before its first use (cudaMemset), and every call leaves
+ *                   the counters zero again, so one buffer serves any later call that
+ *                   fits in it.
+ * num_splits: 0 = load-balanced planner; > 0 = force that many KV splits per sequence
+ * (the kernel-lab Triton semantics: pages_per_split = ceil(max_pages_per_seq / num_splits)).
+ */
+int kl_paged_decode_workspace_size(int dtype, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                   int page_size, int max_pages_per_seq, int num_splits,
+                                   size_t* partial_bytes, size_t* sync_bytes);
+
+/*
+ * Single-token decode attention over a paged KV cache, split-KV with an exact
+ * log-sum-exp merge:  out[b, h] = softmax(scale * q[b, h] . K_b^T) V_b.
+ * Only the first ceil(seq_lens[b] / page_size) block-table entries of row b are read.
+ * seq_lens[b] == 0 yields zeros. num_pages bounds valid page ids (entries outside
+ * [0, num_pages) are skipped and flagged KL_STATUS_BAD_PAGE). The scratch buffers come
+ * from kl_paged_decode_workspace_size; calls that overlap on the GPU need separate
+ * buffers. batch == 0 is a no-op.
+ *
+ * Superset of kernel_lab::launch_paged_decode_attention (csrc/kernel_lab.h:21-33 in
+ * kernel-lab), which is the torch op paged_decode_attention's backend
+ * (csrc/torch_bindings.cpp:71-103): adds the block-table width, the pool size, the
+ * split override and caller-owned scratch. Any head_dim, group size and page size are
+ * accepted (fp16/bf16 with head_dim 64/128/256 run on the tensor-core path).
+ */
+int kl_paged_decode(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                    const int32_t* block_table, const int32_t* seq_lens, int batch, int num_q_heads,
+                    int num_kv_heads, int head_dim, int page_size, int64_t block_table_stride,
+                    int max_pages_per_seq, int64_t num_pages, float scale, int num_splits, void* partials,
+                    size_t partial_bytes, void* sync, size_t sync_bytes, void* stream);
+
+/*
+ * Exactly the argument list of kernel_lab::launch_paged_decode_attention
+ * (csrc/kernel_lab.h:27-33 in kernel-lab). The block-table width is taken to be
+ * block_table_stride and page ids are not range-checked (the pool size is unknown), as
+ * in kernel-lab. Scratch comes from cudaMallocAsync on `stream` and is freed on it.
+ */
+int kl_paged_decode_attention(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                              const int32_t* block_table, const int32_t* seq_lens, int batch,
+                              int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                              int64_t block_table_stride, float scale, void* stream);
+
+/*
+ * Synchronise `stream`, copy status word 0 of a decode sync buffer to *status and,
+ * if clear != 0, reset it to zero.
+ */
+int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KERNEL_LAB_B200_H_ */

@@ -1,0 +1,212 @@
+// Fused residual-add + RMSNorm (and plain RMSNorm) for sm_100a.
+//
+// Replaces the reference's two-pass kernel (csrc/rmsnorm.cu:17-62 in
+// kernel-lab). The hot variant keeps the whole row in registers: one CTA per
+// row, every thread issues all of its 16-byte streaming loads (x and residual)
+// before using any, forms the rounded sum, reduces the sum of squares with one
+// shuffle tree and one shared-memory hop, and writes both outputs. Each tensor
+// therefore crosses HBM exactly once (x, residual in; residual, out out; the
+// weight stays L2-resident), with no second pass over the row.
+//
+// Rounding follows kernel_lab/reference.py:13-30 exactly:
+//   residual' = T(float(x) + float(residual))          (bit-exact)
+//   out       = T((float(residual') * rstd) * float(w)) with rstd = rsqrt(mean(residual'^2) + eps)
+//
+// Rows that are misaligned, of odd width or wider than the register budget use
+// a two-pass fallback that re-reads its own row (from L2) for the output pass.
+#include <algorithm>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernel_lab_b200.h"
+
+namespace klb {
+namespace {
+
+template <typename T>
+struct Pack16 {
+  static constexpr int N = 16 / sizeof(T);
+  union {
+    uint4 raw;
+    T v[N];
+  };
+};
+
+// Sum over the block; every thread gets the total. `red` holds one float per warp.
+__device__ __forceinline__ float block_allreduce_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  v = warp_allreduce_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float total = 0.0f;
+  for (int w = 0; w < nwarps; ++w) total += red[w];
+  return total;
+}
+
+// One CTA per row; each thread owns NPT 16-byte packs of the row, strided by blockDim.
+template <typename T, int NPT, bool RES>
+__global__ void __launch_bounds__(1024) rmsnorm_row_regs(T* __restrict__ out, const T* __restrict__ x,
+                                                         T* __restrict__ residual, const T* __restrict__ weight,
+                                                         int hidden, int64_t x_row_stride, float eps) {
+  using P = Pack16<T>;
+  __shared__ float red[32];
+  const int packs = hidden / P::N;
+  const int64_t row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * x_row_stride);
+  uint4* rr = reinterpret_cast<uint4*>(residual + row * static_cast<int64_t>(hidden));
+  uint4* orow = reinterpret_cast<uint4*>(out + row * static_cast<int64_t>(hidden));
+  const uint4* wr = reinterpret_cast<const uint4*>(weight);
+
+  P a[NPT];
+  P r[NPT];
+#pragma unroll
+  for (int i = 0; i < NPT; ++i) {
+    const int pk = threadIdx.x + i * blockDim.x;
+    if (pk < packs) {
+      a[i].raw = __ldcs(xr + pk);
+      if constexpr (RES) r[i].raw = __ldcs(rr + pk);
+    }
+  }
+
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NPT; ++i) {
+    const int pk = threadIdx.x + i * blockDim.x;
+    if (pk < packs) {
+      if constexpr (RES) {
+#pragma unroll
+        for (int j = 0; j < P::N; ++j) {
+          a[i].v[j] = Storage<T>::store(Storage<T>::load(a[i].v[j]) + Storage<T>::load(r[i].v[j]));
+        }
+        rr[pk] = a[i].raw;
+      }
+#pragma unroll
+      for (int j = 0; j < P::N; ++j) {
+        const float f = Storage<T>::load(a[i].v[j]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+  }
+
+  const float rstd = rsqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
+
+#pragma unroll
+  for (int i = 0; i < NPT; ++i) {
+    const int pk = threadIdx.x + i * blockDim.x;
+    if (pk < packs) {
+      P w, o;
+      w.raw = __ldg(wr + pk);
+#pragma unroll
+      for (int j = 0; j < P::N; ++j) {
+        o.v[j] = Storage<T>::store((Storage<T>::load(a[i].v[j]) * rstd) * Storage<T>::load(w.v[j]));
+      }
+      orow[pk] = o.raw;
+    }
+  }
+}
+
+// General fallback: any width, any alignment. Pass 1 forms (and stores) the rounded
+// sum and the sum of squares; pass 2 re-reads this thread's own elements (L2 hits).
+template <typename T, bool RES>
+__global__ void __launch_bounds__(1024) rmsnorm_row_twopass(T* __restrict__ out, const T* __restrict__ x,
+                                                            T* __restrict__ residual, const T* __restrict__ weight,
+                                                            int hidden, int64_t x_row_stride, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * x_row_stride;
+  T* rr = residual + row * static_cast<int64_t>(hidden);
+  T* orow = out + row * static_cast<int64_t>(hidden);
+
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float f;
+    if constexpr (RES) {
+      const T s = Storage<T>::store(Storage<T>::load(xr[i]) + Storage<T>::load(rr[i]));
+      rr[i] = s;
+      f = Storage<T>::load(s);
+    } else {
+      f = Storage<T>::load(xr[i]);
+    }
+    ss = fmaf(f, f, ss);
+  }
+  const float rstd = rsqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
+  const T* src = RES ? rr : xr;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    orow[i] = Storage<T>::store((Storage<T>::load(src[i]) * rstd) * Storage<T>::load(weight[i]));
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T, int NPT>
+void launch_regs(void* out, const void* x, void* residual, const void* weight, int rows, int hidden,
+                 int64_t x_row_stride, float eps, cudaStream_t stream, int threads) {
+  auto o = static_cast<T*>(out);
+  auto xi = static_cast<const T*>(x);
+  auto r = static_cast<T*>(residual);
+  auto w = static_cast<const T*>(weight);
+  if (residual) {
+    rmsnorm_row_regs<T, NPT, true><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
+  } else {
+    rmsnorm_row_regs<T, NPT, false><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
+  }
+}
+
+template <typename T>
+int launch_typed(void* out, const void* x, void* residual, const void* weight, int rows, int hidden,
+                 int64_t x_row_stride, float eps, cudaStream_t stream) {
+  constexpr int N = 16 / sizeof(T);
+  const bool vec = hidden % N == 0 && x_row_stride % N == 0 && aligned16(out) && aligned16(x) &&
+                   aligned16(weight) && (residual == nullptr || aligned16(residual));
+  const int packs = hidden / N;
+  if (vec && packs <= 8 * 1024) {
+    // Packs per thread: enough to keep >= 4 16-byte loads per tensor in flight on wide
+    // rows, while a row never needs more than 1024 threads.
+    const int npt = packs <= 128 ? 1 : packs <= 512 ? 2 : packs <= 2048 ? 4 : 8;
+    const int threads = std::min(1024, std::max(32, ((packs + npt - 1) / npt + 31) / 32 * 32));
+    switch (npt) {
+      case 1: launch_regs<T, 1>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
+      case 2: launch_regs<T, 2>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
+      case 4: launch_regs<T, 4>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
+      default: launch_regs<T, 8>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
+    }
+  } else {
+    const int threads = std::min(1024, std::max(32, (hidden + 31) / 32 * 32));
+    auto o = static_cast<T*>(out);
+    auto xi = static_cast<const T*>(x);
+    auto r = static_cast<T*>(residual);
+    auto w = static_cast<const T*>(weight);
+    if (residual) {
+      rmsnorm_row_twopass<T, true><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
+    } else {
+      rmsnorm_row_twopass<T, false><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
+    }
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace klb
+
+extern "C" int kl_rms_norm(int dtype, void* out, const void* x, void* residual, const void* weight, int rows,
+                           int hidden, int64_t x_row_stride, float eps, void* stream) {
+  if (rows == 0) return 0;
+  if (rows < 0 || hidden <= 0 || x_row_stride < 0 || !out || !x || !weight) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case KL_FLOAT32:
+      return klb::launch_typed<float>(out, x, residual, weight, rows, hidden, x_row_stride, eps, s);
+    case KL_FLOAT16:
+      return klb::launch_typed<__half>(out, x, residual, weight, rows, hidden, x_row_stride, eps, s);
+    case KL_BFLOAT16:
+      return klb::launch_typed<__nv_bfloat16>(out, x, residual, weight, rows, hidden, x_row_stride, eps, s);
+    default:
+      return static_cast<int>(cudaErrorInvalidValue);
+  }
+}

@@ -1,0 +1,83 @@
+"""Python wrappers for the CUDA kernels (torch.ops.kernel_lab.*).
+
+Same API as kernel-lab's ``kernel_lab/cuda_ops.py:11-61`` (``available``,
+``why_unavailable``, ``rms_norm``, ``fused_add_rms_norm``, ``paged_decode_attention``),
+plus ``num_splits`` on ``paged_decode_attention`` and ``decode_status``. There is no
+fallback: if the extension is not built these functions raise RuntimeError.
+"""
+
+from __future__ import annotations
+
+import torch
+
+try:
+    from kernel_lab import _C  # registers torch.ops.kernel_lab
+
+    _LOADED = True
+    _LOAD_ERROR = ""
+except ImportError as exc:  # not built
+    _LOADED = False
+    _LOAD_ERROR = str(exc)
+
+
+def available() -> bool:
+    return _LOADED and torch.cuda.is_available()
+
+
+def why_unavailable() -> str:
+    if not _LOADED:
+        return f"CUDA extension not built ({_LOAD_ERROR}); run `python kernel-lab_b200/build.py`"
+    return "no CUDA device"
+
+
+def _require() -> None:
+    if not _LOADED:
+        raise RuntimeError(f"kernel_lab: {why_unavailable()}")
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    _require()
+    out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    torch.ops.kernel_lab.rms_norm(out, x, weight, eps)
+    return out
+
+
+def fused_add_rms_norm(
+    x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Functional form: returns (out, new_residual) and leaves ``residual`` untouched.
+    Call torch.ops.kernel_lab.fused_add_rms_norm directly to update in place."""
+    _require()
+    out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    new_residual = residual.contiguous().clone()
+    torch.ops.kernel_lab.fused_add_rms_norm(out, x, new_residual, weight, eps)
+    return out, new_residual
+
+
+def paged_decode_attention(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    num_splits: int | None = None,
+) -> torch.Tensor:
+    """Decode attention over a paged cache. ``num_splits=None`` uses the load-balanced
+    planner; an integer forces that many KV splits per sequence (Triton semantics)."""
+    _require()
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    out = torch.empty_like(q)
+    if num_splits is None:
+        torch.ops.kernel_lab.paged_decode_attention(out, q.contiguous(), k_cache, v_cache, block_table, seq_lens, scale)
+    else:
+        torch.ops.kernel_lab.paged_decode_attention_splits(
+            out, q.contiguous(), k_cache, v_cache, block_table, seq_lens, scale, int(num_splits)
+        )
+    return out
+
+
+def decode_status(clear: bool = False) -> int:
+    """KL_STATUS_* bits left by decode calls on the current device and stream (synchronises)."""
+    _require()
+    return int(_C.decode_status(clear))

@@ -1,0 +1,200 @@
+"""Paged KV-cache pools: the data format on both sides of the decode kernel.
+
+A serving engine keeps every sequence's keys and values in fixed-size pages of
+one pool, NHD layout ``[num_pages, page_size, num_kv_heads, head_dim]``, and a
+block table lists each sequence's pages in order. This module builds such pools.
+
+``random_decode_problem`` / ``build_paged_kv`` reproduce the seeded fixtures of
+kernel_lab/kv_cache.py:33-102 bit for bit (same generator protocol: one
+``torch.Generator().manual_seed(seed)`` drawing q, then every sequence's keys,
+then every sequence's values; a second one drawing the page permutation), so the
+golden vectors produced by the reference apply to them. Two differences, both
+deliberate: the spare-page poison is a parameter (default NaN, so a kernel that
+reads a page it should not turns the output into NaN, not merely "large"), and
+the scatter is vectorised instead of a per-page loop.
+
+``random_paged_pool`` builds the large serving-scale pools for the benchmark
+directly on the device (same layout and page shuffling, values from a CUDA
+generator), because drawing gigabytes on the host would take minutes.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+NAN = float("nan")
+
+
+@dataclass
+class PagedKV:
+    k_cache: torch.Tensor  # [num_pages, page_size, num_kv_heads, head_dim]
+    v_cache: torch.Tensor
+    block_table: torch.Tensor  # [batch, max_pages] int32, padded with page 0
+    seq_lens: torch.Tensor  # [batch] int32
+    page_size: int
+
+    @property
+    def max_pages(self) -> int:
+        return self.block_table.shape[1]
+
+    @property
+    def num_pages(self) -> int:
+        return self.k_cache.shape[0]
+
+
+def pages_for(seq_len: int, page_size: int) -> int:
+    return (seq_len + page_size - 1) // page_size
+
+
+def _page_order(total: int, seed: int) -> torch.Tensor:
+    return torch.randperm(total, generator=torch.Generator().manual_seed(seed))
+
+
+def build_paged_kv(
+    keys: list[torch.Tensor],
+    values: list[torch.Tensor],
+    page_size: int,
+    extra_pages: int = 3,
+    seed: int = 0,
+    poison: float = NAN,
+) -> PagedKV:
+    """Scatter per-sequence K/V (``[L, Hkv, D]`` each) into shuffled pages of one pool.
+
+    Pages are handed out in the order of a seeded permutation of the pool; the
+    ``extra_pages`` pages left over are filled with ``poison``; the unused tail of
+    a sequence's last page is zero; block-table padding is page id 0.
+    """
+    if not keys or len(keys) != len(values):
+        raise ValueError("need one K and one V tensor per sequence")
+    _, num_kv_heads, head_dim = keys[0].shape
+    lens = [k.shape[0] for k in keys]
+    if min(lens) < 1:
+        raise ValueError("every sequence needs at least one cached token")
+    needed = [pages_for(n, page_size) for n in lens]
+    used = sum(needed)
+    total = used + extra_pages
+    device, dtype = keys[0].device, keys[0].dtype
+
+    order = _page_order(total, seed)
+    table = torch.zeros((len(keys), max(needed)), dtype=torch.int32)
+    starts = torch.tensor([0, *needed[:-1]]).cumsum(0)
+    for b, n in enumerate(needed):
+        table[b, :n] = order[starts[b] : starts[b] + n].to(torch.int32)
+
+    # Destination (page, slot) of every token, all sequences concatenated.
+    tok_page = torch.cat([table[b, torch.arange(n) // page_size].long() for b, n in enumerate(lens)])
+    tok_slot = torch.cat([torch.arange(n) % page_size for n in lens])
+
+    k_cache = torch.full((total, page_size, num_kv_heads, head_dim), poison, dtype=dtype, device=device)
+    v_cache = torch.full_like(k_cache, poison)
+    assigned = order[:used].to(device)
+    k_cache[assigned] = 0  # partial-page tails: valid memory, never attended
+    v_cache[assigned] = 0
+    k_cache[tok_page.to(device), tok_slot.to(device)] = torch.cat(keys)
+    v_cache[tok_page.to(device), tok_slot.to(device)] = torch.cat(values)
+    return PagedKV(
+        k_cache=k_cache,
+        v_cache=v_cache,
+        block_table=table.to(device),
+        seq_lens=torch.tensor(lens, dtype=torch.int32, device=device),
+        page_size=page_size,
+    )
+
+
+def random_decode_problem(
+    seq_lens: list[int],
+    num_q_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    page_size: int,
+    dtype: torch.dtype = torch.float16,
+    device: str = "cpu",
+    seed: int = 0,
+    poison: float = NAN,
+) -> tuple[torch.Tensor, PagedKV, list[torch.Tensor], list[torch.Tensor]]:
+    """A seeded query batch and its paged cache, plus the contiguous K/V it came from.
+
+    Values are N(0, 1) drawn in float32 on the host and rounded to ``dtype``.
+    """
+    generator = torch.Generator().manual_seed(seed)
+
+    def rand(*shape: int) -> torch.Tensor:
+        return torch.randn(*shape, generator=generator).to(device=device, dtype=dtype)
+
+    q = rand(len(seq_lens), num_q_heads, head_dim)
+    keys = [rand(n, num_kv_heads, head_dim) for n in seq_lens]
+    values = [rand(n, num_kv_heads, head_dim) for n in seq_lens]
+    return q, build_paged_kv(keys, values, page_size, seed=seed, poison=poison), keys, values
+
+
+def random_paged_pool(
+    seq_lens: list[int],
+    num_q_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    page_size: int,
+    dtype: torch.dtype = torch.bfloat16,
+    device: str | torch.device = "cuda",
+    seed: int = 0,
+    extra_pages: int = 3,
+    poison: float = NAN,
+    kv_head_slice: tuple[int, int] | None = None,
+) -> tuple[torch.Tensor, PagedKV]:
+    """Serving-scale pool generated on ``device``: N(0,1) q/K/V, shuffled pages, poisoned spares.
+
+    ``kv_head_slice=(lo, hi)`` keeps only KV heads ``lo..hi-1`` (and their query
+    groups) of the full problem, as one tensor-parallel rank holds them. Every
+    rank draws the same full-size random stream per page, so the union of the
+    shards is the unsharded problem.
+    """
+    dev = torch.device(device)
+    lens = [int(n) for n in seq_lens]
+    needed = [pages_for(n, page_size) for n in lens]
+    used = sum(needed)
+    total = used + extra_pages
+    lo, hi = kv_head_slice if kv_head_slice is not None else (0, num_kv_heads)
+    group = num_q_heads // num_kv_heads
+
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    q_full = torch.randn(len(lens), num_q_heads, head_dim, generator=gen, device=dev, dtype=torch.float32)
+    q = q_full[:, lo * group : hi * group].to(dtype).contiguous()
+
+    shape = (total, page_size, hi - lo, head_dim)
+    k_cache = torch.empty(shape, dtype=dtype, device=dev)
+    v_cache = torch.empty(shape, dtype=dtype, device=dev)
+    # Draw page-sized blocks of the full-width pool and keep this rank's heads, in
+    # chunks so the float32 staging buffer stays small.
+    chunk = max(1, (1 << 28) // (page_size * num_kv_heads * head_dim * 4))
+    for start in range(0, total, chunk):
+        stop = min(total, start + chunk)
+        for cache in (k_cache, v_cache):
+            block = torch.randn(
+                stop - start, page_size, num_kv_heads, head_dim, generator=gen, device=dev, dtype=torch.float32
+            )
+            cache[start:stop] = block[:, :, lo:hi].to(dtype)
+            del block
+
+    order = _page_order(total, seed).to(dev)
+    width = max(needed)
+    table = torch.zeros((len(lens), width), dtype=torch.int32, device=dev)
+    starts = torch.tensor([0, *needed[:-1]], device=dev).cumsum(0)
+    cols = torch.arange(width, device=dev)
+    need_t = torch.tensor(needed, device=dev)
+    mask = cols[None, :] < need_t[:, None]
+    src = (starts[:, None] + cols[None, :]).clamp(max=max(used - 1, 0))
+    table = torch.where(mask, order[src].to(torch.int32), table)
+
+    spare = order[used:]
+    k_cache[spare] = poison
+    v_cache[spare] = poison
+    # Zero the unused tail of each sequence's last page.
+    for b, n in enumerate(lens):
+        tail = n % page_size
+        if tail:
+            page = int(order[int(starts[b]) + needed[b] - 1])
+            k_cache[page, tail:] = 0
+            v_cache[page, tail:] = 0
+    seq = torch.tensor(lens, dtype=torch.int32, device=dev)
+    return q, PagedKV(k_cache=k_cache, v_cache=v_cache, block_table=table, seq_lens=seq, page_size=page_size)

@@ -1,0 +1,131 @@
+"""NumPy restatement of kernel-lab's fp32 reference math (TEST INFRASTRUCTURE ONLY).
+
+This module is the checker for the CUDA kernels and the timed CPU baseline in
+``bench.py``. It is not part of the product and is never called by it.
+
+Parity is pinned: ``tests/test_oracle.py`` checks every function here against the
+golden vectors in ``tests/golden/``, which ``tests/golden/make_golden.py``
+produced by running the reference's own ``kernel_lab/reference.py`` and
+``kernel_lab/kv_cache.py`` (PyTorch, CPU) on seeded inputs.
+
+Arrays are NumPy float32 holding values that are exactly representable in the
+storage dtype ("f32", "f16" or "bf16"), because NumPy has no bfloat16. The
+functions round to the storage dtype at the same points as the reference: the
+residual stream after the add, and every output (kernel_lab/reference.py:1-6).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+DTYPES = ("f32", "f16", "bf16")
+ELEM_BYTES = {"f32": 4, "f16": 2, "bf16": 2}
+LOG2E = 1.4426950408889634
+
+
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float32 values to ``dtype`` with round-to-nearest-even; return float32.
+
+    fp16 uses NumPy's IEEE half. bf16 keeps the top 16 bits of the float32 pattern
+    after adding half an ulp plus the tie-to-even bit; NaN stays NaN.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "f32":
+        return x.copy()
+    if dtype == "f16":
+        return x.astype(np.float16).astype(np.float32)
+    if dtype != "bf16":
+        raise ValueError(f"unknown dtype {dtype!r}")
+    bits = x.view(np.uint32).astype(np.uint64)
+    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    out = rounded.view(np.float32).copy()
+    nan = np.isnan(x)
+    out[nan] = np.float32("nan")
+    return out
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    """uint16 bfloat16 bit patterns -> float32 values."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> uint16 bfloat16 bit patterns (round to nearest even)."""
+    return (round_to(x, "bf16").view(np.uint32) >> 16).astype(np.uint16)
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float = 1e-6, dtype: str = "f32") -> np.ndarray:
+    """y = x / sqrt(mean(x^2) + eps) * weight over the last axis, fp32 math, rounded to dtype.
+
+    Follows kernel_lab/reference.py:13-17: the product is formed as (x * rstd) * w.
+    """
+    xf = np.asarray(x, dtype=np.float32)
+    ms = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
+    rstd = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    return round_to((xf * rstd) * np.asarray(weight, dtype=np.float32), dtype)
+
+
+def fused_add_rms_norm(
+    x: np.ndarray, residual: np.ndarray, weight: np.ndarray, eps: float = 1e-6, dtype: str = "f32"
+) -> tuple[np.ndarray, np.ndarray]:
+    """Pre-norm step: new_residual = dtype(x + residual); out = rms_norm(new_residual).
+
+    Follows kernel_lab/reference.py:20-30. The sum is formed in fp32 and rounded
+    once to the storage dtype, so the residual output is bit-exact.
+    """
+    new_residual = round_to(np.asarray(x, np.float32) + np.asarray(residual, np.float32), dtype)
+    return rms_norm(new_residual, weight, eps, dtype), new_residual
+
+
+def paged_decode_attention(
+    q: np.ndarray,
+    k_cache: np.ndarray,
+    v_cache: np.ndarray,
+    block_table: np.ndarray,
+    seq_lens: np.ndarray,
+    scale: float | None = None,
+    dtype: str = "f32",
+) -> np.ndarray:
+    """Single-token GQA decode attention over a paged KV cache (NHD layout), fp32 math.
+
+    Follows kernel_lab/reference.py:33-68:
+        q            [batch, num_q_heads, head_dim]
+        k/v_cache    [num_pages, page_size, num_kv_heads, head_dim]
+        block_table  [batch, >= ceil(len/page_size)] int32 page ids, in order
+        seq_lens     [batch] int32
+    Only the first ceil(len / page_size) block-table entries of a row are read,
+    so spare (poisoned) pages and padding never enter the result. A sequence of
+    length 0 yields zeros, as the reference's empty einsum does.
+    """
+    q = np.asarray(q, dtype=np.float32)
+    batch, num_q_heads, head_dim = q.shape
+    _, page_size, num_kv_heads, _ = k_cache.shape
+    group = num_q_heads // num_kv_heads
+    scale = head_dim**-0.5 if scale is None else scale
+    out = np.zeros_like(q)
+    for b in range(batch):
+        length = max(int(seq_lens[b]), 0)
+        if length == 0:
+            continue
+        pages = np.asarray(block_table[b, : (length + page_size - 1) // page_size], dtype=np.int64)
+        k = np.asarray(k_cache[pages], np.float32).reshape(-1, num_kv_heads, head_dim)[:length]
+        v = np.asarray(v_cache[pages], np.float32).reshape(-1, num_kv_heads, head_dim)[:length]
+        # [L, Hkv, D] -> [Hkv, L, D]; query heads grouped per KV head: [Hkv, G, D].
+        k = np.ascontiguousarray(k.transpose(1, 0, 2))
+        v = np.ascontiguousarray(v.transpose(1, 0, 2))
+        qb = q[b].reshape(num_kv_heads, group, head_dim)
+        scores = np.matmul(qb, k.transpose(0, 2, 1)) * np.float32(scale)  # [Hkv, G, L]
+        scores -= scores.max(axis=-1, keepdims=True)
+        probs = np.exp(scores, dtype=np.float32)
+        probs /= probs.sum(axis=-1, keepdims=True, dtype=np.float32)
+        out[b] = np.matmul(probs, v).reshape(num_q_heads, head_dim)
+    return round_to(out, dtype)
+
+
+def decode_bytes(seq_lens, num_q_heads: int, num_kv_heads: int, head_dim: int, elem_bytes: int) -> int:
+    """Algorithmic HBM bytes of one decode call: K and V read once, q read and out written once.
+
+    Same count as kernel_lab/bench/roofline.py:76-84; block table and seq_lens are not counted.
+    """
+    tokens = int(np.sum(np.maximum(np.asarray(seq_lens, dtype=np.int64), 0)))
+    return 2 * tokens * num_kv_heads * head_dim * elem_bytes + 2 * len(seq_lens) * num_q_heads * head_dim * elem_bytes

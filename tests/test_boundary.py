@@ -1,0 +1,123 @@
+"""The drop-in boundary, checked without a GPU.
+
+* libkernel_lab_b200.so loads and exports every function ``include/kernel_lab_b200.h`` declares;
+* calls that need no device (no-ops, argument validation) answer correctly;
+* ``import kernel_lab._C`` registers kernel-lab's exact ``torch.ops.kernel_lab`` schemas
+  (csrc/torch_bindings.cpp:107-113 there) and Meta kernels for tracing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+import pytest
+import torch
+
+from tests.conftest import REPO
+
+HEADER = REPO / "include" / "kernel_lab_b200.h"
+CUDA_ERROR_INVALID_VALUE = 1
+
+
+def declared_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(kl_\w+)\s*\(", text, flags=re.M)
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert names == [
+        "kl_version",
+        "kl_status_string",
+        "kl_rms_norm",
+        "kl_paged_decode_workspace_size",
+        "kl_paged_decode",
+        "kl_paged_decode_attention",
+        "kl_paged_decode_read_status",
+    ]
+
+
+def test_library_exports_every_declared_symbol():
+    from kernel_lab import capi
+
+    lib = capi.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert set(capi.SIGNATURES) == set(declared_functions())
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r" T (kl_\w+)$", nm.stdout, flags=re.M))
+    assert set(declared_functions()) <= exported
+
+
+def test_version_and_status_strings():
+    from kernel_lab import capi
+
+    assert capi.version().startswith("kernel_lab_b200 ") and "sm_100a" in capi.version()
+    assert capi.status_string(0) == "success"
+    assert "invalid" in capi.status_string(CUDA_ERROR_INVALID_VALUE).lower()
+
+
+def test_noop_and_validation_without_a_device():
+    from kernel_lab import capi
+
+    lib = capi.load()
+    # rows == 0 and batch == 0 are no-ops (kernel-lab rmsnorm.cu:102, paged_attention.cu:187).
+    assert lib.kl_rms_norm(2, None, None, None, None, 0, 4096, 4096, 1e-5, None) == 0
+    assert lib.kl_paged_decode(2, *([None] * 6), 0, 32, 8, 128, 16, 4, 4, 10, 0.1, 0, None, 0, None, 0, None) == 0
+    # Bad arguments are rejected before anything touches a device.
+    assert lib.kl_rms_norm(2, None, None, None, None, 4, 4096, 4096, 1e-5, None) == CUDA_ERROR_INVALID_VALUE
+    assert lib.kl_rms_norm(7, 1, 1, None, 1, 4, 4096, 4096, 1e-5, None) == CUDA_ERROR_INVALID_VALUE
+    assert lib.kl_paged_decode(2, *([None] * 6), 4, 32, 8, 128, 16, 4, 4, 10, 0.1, 0, None, 0, None, 0, None) == (
+        CUDA_ERROR_INVALID_VALUE
+    )
+    size = ctypes.c_size_t(1)
+    assert lib.kl_paged_decode_workspace_size(2, 0, 32, 8, 128, 16, 4, 0, ctypes.byref(size), ctypes.byref(size)) == 0
+    assert lib.kl_paged_decode_read_status(None, None, 0, None) == CUDA_ERROR_INVALID_VALUE
+
+
+# kernel-lab's schema strings, verbatim (csrc/torch_bindings.cpp:108-113 there).
+REFERENCE_SCHEMAS = {
+    "rms_norm": "rms_norm(Tensor! out, Tensor x, Tensor weight, float eps) -> ()",
+    "fused_add_rms_norm": "fused_add_rms_norm(Tensor! out, Tensor x, Tensor! residual, Tensor weight, float eps) -> ()",
+    "paged_decode_attention": (
+        "paged_decode_attention(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, "
+        "Tensor block_table, Tensor seq_lens, float scale) -> ()"
+    ),
+}
+
+
+def test_torch_ops_have_the_reference_schemas():
+    from kernel_lab import _C, cuda_ops  # noqa: F401
+
+    for name, schema in REFERENCE_SCHEMAS.items():
+        op = getattr(torch.ops.kernel_lab, name)
+        assert str(op.default._schema) == str(torch._C.parse_schema("kernel_lab::" + schema))
+    assert "num_splits" in str(torch.ops.kernel_lab.paged_decode_attention_splits.default._schema)
+    assert cuda_ops._LOADED
+
+
+def test_meta_kernels_trace_without_a_device():
+    from kernel_lab import _C  # noqa: F401
+
+    x = torch.empty(4, 256, device="meta", dtype=torch.float16)
+    w = torch.empty(256, device="meta", dtype=torch.float16)
+    out = torch.empty_like(x)
+    torch.ops.kernel_lab.rms_norm(out, x, w, 1e-6)
+    torch.ops.kernel_lab.fused_add_rms_norm(out, x, torch.empty_like(x), w, 1e-6)
+    q = torch.empty(2, 8, 64, device="meta", dtype=torch.bfloat16)
+    kc = torch.empty(4, 16, 2, 64, device="meta", dtype=torch.bfloat16)
+    bt = torch.empty(2, 2, device="meta", dtype=torch.int32)
+    ln = torch.empty(2, device="meta", dtype=torch.int32)
+    torch.ops.kernel_lab.paged_decode_attention(torch.empty_like(q), q, kc, kc, bt, ln, 0.125)
+
+
+def test_cuda_ops_fail_loudly_without_a_device():
+    from kernel_lab import cuda_ops
+
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    assert not cuda_ops.available()
+    with pytest.raises(RuntimeError):
+        cuda_ops.rms_norm(torch.randn(2, 8), torch.ones(8))

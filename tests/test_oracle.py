@@ -1,0 +1,139 @@
+"""The oracle is the ground truth for the kernels, so it is pinned to the reference itself.
+
+Golden vectors in tests/golden/ were produced by kernel-lab's own ``reference.py`` and
+``kv_cache.py`` (tests/golden/make_golden.py). Here the NumPy oracle must reproduce them,
+and this repository's fixture builder must reproduce the reference's inputs bit for bit.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests.conftest import (
+    DT,
+    build_decode_case,
+    golden_array,
+    golden_index,
+    golden_to_torch,
+    make_rms_inputs,
+    sha,
+    to_f32_numpy,
+)
+
+DECODE_CASES = [c["name"] for c in golden_index()["decode"]]
+RMS_CASES = [c["name"] for c in golden_index()["rmsnorm"]]
+ORACLE_TOL = {"f32": 1e-5, "f16": 1e-3, "bf16": 8e-3}
+
+
+def _decode(name):
+    return next(c for c in golden_index()["decode"] if c["name"] == name)
+
+
+def _rms(name):
+    return next(c for c in golden_index()["rmsnorm"] if c["name"] == name)
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+def test_builder_reproduces_reference_inputs(name):
+    case = _decode(name)
+    q, kv, _, _ = build_decode_case(case, poison=1e4)
+    got = {
+        "q": sha(q),
+        "k_cache": sha(kv.k_cache),
+        "v_cache": sha(kv.v_cache),
+        "block_table": sha(kv.block_table),
+        "seq_lens": sha(kv.seq_lens),
+    }
+    assert got == case["in_sha256"]
+
+
+@pytest.mark.parametrize("name", DECODE_CASES)
+def test_oracle_decode_matches_reference(name):
+    case = _decode(name)
+    q, kv, _, _ = build_decode_case(case)  # NaN-poisoned spares: never read
+    got = oracle.paged_decode_attention(
+        to_f32_numpy(q), to_f32_numpy(kv.k_cache), to_f32_numpy(kv.v_cache), kv.block_table.numpy(),
+        kv.seq_lens.numpy(), case.get("scale"), case["dt"],
+    )
+    want = golden_to_torch(golden_array("decode", f"{name}/out"), case["dt"]).float().numpy()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, atol=ORACLE_TOL[case["dt"]], rtol=ORACLE_TOL[case["dt"]])
+
+
+def test_oracle_known_answer_one_hot_key():
+    """One key far more aligned than the rest and v[t] = t: the output is 13.0 (reference test
+    tests/test_paged_attention.py:81-91)."""
+    from kernel_lab.kv_cache import build_paged_kv
+
+    d = 32
+    keys = [torch.zeros(20, 1, d)]
+    values = [torch.arange(20, dtype=torch.float32)[:, None, None].expand(20, 1, d).clone()]
+    keys[0][13, 0, 0] = 100.0
+    kv = build_paged_kv(keys, values, page_size=16, poison=1e4)
+    assert {
+        "k_cache": sha(kv.k_cache),
+        "v_cache": sha(kv.v_cache),
+        "block_table": sha(kv.block_table),
+    } == golden_index()["onehot"]["in_sha256"]
+    q = np.zeros((1, 1, d), np.float32)
+    q[0, 0, 0] = 1.0
+    out = oracle.paged_decode_attention(
+        q, kv.k_cache.numpy(), kv.v_cache.numpy(), kv.block_table.numpy(), kv.seq_lens.numpy(), scale=1.0
+    )
+    np.testing.assert_allclose(out, golden_array("decode", "onehot/out"), atol=1e-5)
+    np.testing.assert_allclose(out, 13.0, atol=1e-4)
+
+
+@pytest.mark.parametrize("name", RMS_CASES)
+def test_oracle_rmsnorm_matches_reference(name):
+    case = _rms(name)
+    dt = case["dt"]
+    x, r, w = make_rms_inputs(case["shape"], DT[dt])
+    assert {"x": sha(x), "residual": sha(r), "weight": sha(w)} == case["in_sha256"]
+    out, new_res = oracle.fused_add_rms_norm(to_f32_numpy(x), to_f32_numpy(r), to_f32_numpy(w), case["eps"], dt)
+    plain = oracle.rms_norm(to_f32_numpy(x), to_f32_numpy(w), case["eps"], dt)
+    # Residual: bit-exact against the reference's hash.
+    assert sha(torch.from_numpy(new_res).to(DT[dt])) == case["residual_out_sha256"]
+    tol = {"f32": 1e-5, "f16": 2e-3, "bf16": 1.6e-2}[dt]
+    if "sample_rows" in case:
+        rows = case["sample_rows"]
+        h = case["shape"][-1]
+        want = golden_to_torch(golden_array("rmsnorm", f"{name}/out_rows"), dt).float().numpy()
+        want_plain = golden_to_torch(golden_array("rmsnorm", f"{name}/out_plain_rows"), dt).float().numpy()
+        np.testing.assert_allclose(out.reshape(-1, h)[rows], want, atol=tol, rtol=tol)
+        np.testing.assert_allclose(plain.reshape(-1, h)[rows], want_plain, atol=tol, rtol=tol)
+    else:
+        want = golden_to_torch(golden_array("rmsnorm", f"{name}/out"), dt).float().numpy()
+        want_plain = golden_to_torch(golden_array("rmsnorm", f"{name}/out_plain"), dt).float().numpy()
+        np.testing.assert_allclose(out, want, atol=tol, rtol=tol)
+        np.testing.assert_allclose(plain, want_plain, atol=tol, rtol=tol)
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = torch.randn(10000) * 10
+    x = torch.cat([x, torch.tensor([0.0, -0.0, float("inf"), float("-inf"), 1e-40, 3.0e38])])
+    got = oracle.round_to(x.numpy(), "bf16")
+    want = x.to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(got, want)
+    assert np.isnan(oracle.round_to(np.array([np.nan], np.float32), "bf16")).all()
+    bits = oracle.f32_to_bf16_bits(x.numpy())
+    np.testing.assert_array_equal(bits, x.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16))
+
+
+def test_oracle_zero_length_sequence_gives_zeros():
+    """kernel-lab's reference returns zeros for an empty sequence (empty einsum)."""
+    q = np.ones((2, 2, 8), np.float32)
+    k = np.ones((2, 16, 1, 8), np.float32)
+    bt = np.array([[0], [1]], np.int32)
+    out = oracle.paged_decode_attention(q, k, k, bt, np.array([0, 5], np.int32))
+    assert (out[0] == 0).all() and np.allclose(out[1], 1.0)
+
+
+def test_decode_bytes_model():
+    """The roofline's algorithmic bytes (kernel-lab tests/test_roofline.py:23-26)."""
+    assert oracle.decode_bytes([10, 20], 4, 2, 8, 2) == 2 * 30 * 2 * 8 * 2 + 2 * 2 * 4 * 8 * 2
+    # Config 3 headline: batch 64, context 4096, Llama-3-8B heads, bf16.
+    assert oracle.decode_bytes([4096] * 64, 32, 8, 128, 2) == 1_074_790_400
