@@ -52,6 +52,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--workload", choices=["decode", "decode70b", "rmsnorm"], default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, help="override the workload's batch (per GPU for weak scaling)")
+    ap.add_argument("--ctx", type=int, help="override the workload's context length")
     return ap.parse_args()
 
 
@@ -238,6 +240,15 @@ def main() -> None:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     spec = workload_spec(args.workload, world)
+    if args.batch and spec["kind"] == "decode":
+        spec["batch"] = args.batch * (world if spec["scaling"] == "weak" else 1)
+        spec["desc"] += f" (batch overridden: {args.batch})"
+    if args.ctx and spec["kind"] == "decode":
+        spec["ctx"] = args.ctx
+        spec["desc"] += f" (ctx overridden: {args.ctx})"
+    if args.batch and spec["kind"] == "rmsnorm":
+        spec["rows"] = args.batch
+        spec["desc"] += f" (rows overridden: {args.batch})"
     if args.impl == "reference":
         run_reference(args, spec)
         return

@@ -47,6 +47,16 @@ def cuda_home() -> Path:
     return Path("/usr/local/cuda")
 
 
+def host_cxx() -> str:
+    """The C++ compiler for the torch extension. It must link libstdc++ dynamically, like
+    torch itself: a toolchain that links it statically gives the extension a second copy of
+    the iostream/locale state, and formatting a TORCH_CHECK message then crashes."""
+    for cand in (os.environ.get("KL_CXX"), "/usr/bin/g++", os.environ.get("CXX"), "g++"):
+        if cand and shutil.which(cand):
+            return cand
+    raise RuntimeError("no C++ compiler found")
+
+
 def ext_module_path() -> Path:
     return OUT_DIR / f"_C{sysconfig.get_config_var('EXT_SUFFIX')}"
 
@@ -94,7 +104,7 @@ def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
         return target
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     cmd = [
-        os.environ.get("CXX", "g++"),
+        host_cxx(),
         "-O2",
         "-std=c++17",
         "-fPIC",

@@ -6,25 +6,31 @@
 // (kernel_lab/triton_kernels/paged_attention.py:37-173): partial outputs are normalised,
 // carry a base-2 LSE, and an empty split has lse = -inf and zero weight.
 //
-// Work decomposition. The unit of work is a 16-token "tile" of one (sequence, KV head).
-// Every CTA computes the same plan from seq_lens (no host sync): the tiles of all
-// (sequence, KV head) pairs are laid end to end, and CTA c takes the contiguous range
-// [c*R, (c+1)*R) with R = max(min_tiles, ceil(total / grid)). Every CTA therefore streams
-// the same number of KV bytes whatever the length distribution (ragged batches included).
-// A (sequence, KV head) that a range boundary cuts is a "chunk": the CTA writes a
-// normalised fp32 partial and its LSE to scratch and bumps an arrival counter; the CTA
-// that arrives last merges all chunks (no waiting on other CTAs) and resets the counter.
-// A forced split count (num_splits > 0) instead gives every sequence exactly
-// ceil(max_pages / pages_per_split) splits, including empty ones, like the Triton kernel.
+// Work decomposition. A "tile" is 16 tokens of one sequence for one "unit" of heads: a
+// block of HT consecutive KV heads in the tensor-core kernel, one KV head in the generic
+// one. Every CTA computes the same plan from seq_lens (no host sync): the tiles of all
+// (sequence, unit) pairs are laid end to end and CTA c takes the contiguous range
+// [c*R, (c+1)*R), R = max(min_tiles, ceil(total / grid)), so every CTA streams the same
+// number of KV bytes whatever the length distribution (ragged batches included). A
+// (sequence, unit) that a range boundary cuts is split into "chunks": each chunk writes
+// a normalised fp32 partial and its LSE to scratch and bumps an arrival counter; the
+// last chunk to arrive merges them all (nobody waits on another CTA) and resets the
+// counter to zero. A forced split count (num_splits > 0) instead gives every sequence
+// exactly ceil(max_pages / pages_per_split) chunks, including empty ones, like the
+// Triton kernel.
 //
-// Tensor-core kernel (fp16/bf16, head_dim 64/128/256, page size 8 or a multiple of 16):
-// one producer warp walks the plan and issues 2-D TMA loads of each tile's K and V rows
-// (block-table indirection, 128-byte swizzle, L2 evict-first) into a ring of shared-memory
-// stages guarded by mbarriers; four consumer warps take tiles round-robin. A consumer warp
-// computes S = K.Q^T with mma.m16n8k16 (M = 16 tokens, N = 8 query heads of the group,
-// K = head_dim), does the online softmax in base 2 on the fp32 fragments, turns P into
-// the B operand with movmatrix, and accumulates O^T += V^T.P^T (V^T via ldmatrix.trans).
-// Partial results of the consumer warps are combined through shared memory.
+// Tensor-core kernel (fp16/bf16, head_dim 64/128/256, page size 8 or a multiple of 16).
+// A stage holds the K and V rows of one tile for HT KV heads: with Llama-3-8B's 8 KV
+// heads that is one whole 16-token page, 32 KB of K and 32 KB of V read contiguously,
+// instead of 256-byte per-head rows scattered over the page. One producer warp walks the
+// plan and its 32 lanes issue the stage's 2-D TMA boxes (64 columns x 16 rows, 128-byte
+// swizzle, L2 evict-first) into a ring of shared-memory stages guarded by mbarriers.
+// Eight consumer warps: warp (ht, hg, tw) owns KV head ht of the stage and query-head
+// group hg (8*NT query heads of that KV head's GQA group); when a unit has fewer heads
+// than warps, TW warps split the tiles and combine through shared memory. A consumer
+// computes S = K.Q^T with mma.m16n8k16 (M = 16 tokens, N = 8 query heads, K = head_dim),
+// the online softmax in base 2 on the fp32 fragments, turns P into the B operand with
+// movmatrix, and accumulates O^T += V^T.P^T (V^T via ldmatrix.trans).
 //
 // Generic kernel (fp32, other head_dims / page sizes / groups): same plan and merge, CUDA
 // cores, 32-token chunks staged through shared memory.
@@ -39,7 +45,7 @@
 #include <climits>
 #include <cmath>
 #include <cstdint>
-#include <cstring>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -49,12 +55,13 @@
 
 namespace klb {
 
-constexpr int kTile = 16;          // tokens per tile: the MMA's M
-constexpr int kCW = 4;             // consumer warps (tensor-core kernel)
+constexpr int kTile = 16;         // tokens per tile: the MMA's M
+constexpr int kCW = 8;            // consumer warps of the tensor-core kernel
 constexpr int kTCThreads = 32 * (kCW + 1);
 constexpr int kGenThreads = 128;
-constexpr int kGenChunk = 32;      // tokens per step of the generic kernel
-constexpr int kMaxBatch = 16384;   // the plan lives in shared memory
+constexpr int kGenChunk = 32;     // tokens per step of the generic kernel
+constexpr int kMaxBatch = 16384;  // the plan lives in shared memory
+constexpr int kMaxHeadGroups = 4; // query-head groups per KV head (counter stride)
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 struct DecodeArgs {
@@ -67,14 +74,23 @@ struct DecodeArgs {
   int batch, num_q_heads, num_kv_heads, group, head_dim, page_size;
   int64_t bt_stride;
   int max_pages;
-  int64_t num_pages;  // < 0: unknown, page ids not range-checked
+  int64_t num_pages;    // < 0: unknown, page ids not range-checked
   float scale_log2;
+  int units;            // work units per sequence (head blocks or KV heads)
   int splits;           // 0: balanced plan; > 0: forced splits per sequence
   int pages_per_split;  // forced mode
   int min_tiles;        // balanced mode: minimum tiles per CTA
-  uint32_t* sync;       // [0] status, [1 + b * Hkv + kvh] arrival counters
-  float* part_o;        // [slot][group][head_dim]
-  float* part_lse;      // [slot][group]
+  uint32_t* sync;       // [0] status, [1 + (b*Hkv + kvh)*kMaxHeadGroups + hg] arrival counters
+  float* part_o;        // [slot][slot_heads][head_dim]
+  float* part_lse;      // [slot][slot_heads]
+};
+
+struct TcShape {
+  int nstage;  // ring stages
+  int p_rows;  // rows of one TMA box: min(page_size, 16)
+  int ht;      // KV heads per tile
+  int hg;      // query-head groups (of 8*NT heads) per KV head
+  int tw;      // warps splitting the tiles of one (head, group)
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -86,12 +102,12 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // ------------------------------------------------------------------------- plan
 
 struct Seg {
-  int b, kvh;
+  int b, u;                // sequence, unit
   int tok_begin, tok_end;  // token range; empty when tok_end <= tok_begin
-  int slot;                // partial slot of this chunk (unused when whole)
-  int nchunks;             // chunks of this (sequence, KV head)
+  int chunk;               // chunk id of this piece (partial slots derive from it)
+  int nchunks;             // chunks of this (sequence, unit)
   int c_first;             // balanced mode: CTA holding the first chunk
-  bool first_aligned;      // balanced mode: first chunk starts its CTA's range
+  bool first_aligned;      // balanced mode: the first chunk starts its CTA's range
   bool whole;
 };
 
@@ -111,8 +127,8 @@ __device__ __forceinline__ int clamp_len(const DecodeArgs& a, int b, bool report
 }
 
 // All threads of the block. lens[b] = clamped length; prefix[b] = tiles of sequences
-// before b (balanced mode); misc[0] = total tiles over all KV heads, misc[1] = R.
-// misc[4..35] is scan scratch. Ends with a block barrier.
+// before b; misc[0] = total tiles over all units, misc[1] = R; misc[2] (abort flag) and
+// misc[3] are zeroed; misc[4..35] is scan scratch. Ends with a block barrier.
 __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* misc) {
   const int B = a.batch;
   const int nt = blockDim.x;
@@ -126,7 +142,6 @@ __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* mis
     lens[i] = len;
     local += (len + kTile - 1) / kTile;
   }
-  // Block-wide exclusive scan of `local`.
   int inc = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -145,7 +160,7 @@ __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* mis
       if (lane >= o) vi += u;
     }
     if (lane < nw) wtot[lane] = vi - v;
-    if (lane == 31) misc[2] = vi;  // total tiles of one KV head
+    if (lane == 31) misc[2] = vi;  // tiles of one unit, all sequences
   }
   __syncthreads();
   int run = wtot[warp] + inc - local;
@@ -154,13 +169,13 @@ __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* mis
     run += (lens[i] + kTile - 1) / kTile;
   }
   if (tid == 0) {
-    const int per_head = misc[2];
-    prefix[B] = per_head;
-    const int total = per_head * a.num_kv_heads;
+    const int per_unit = misc[2];
+    prefix[B] = per_unit;
+    const int total = per_unit * a.units;
     misc[0] = total;
-    misc[1] = max(a.min_tiles, (total + (int)gridDim.x - 1) / (int)gridDim.x);
-    misc[2] = 0;  // abort flag from here on
-    misc[3] = 0;  // "last arrival" flag
+    misc[1] = max(a.min_tiles, (total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x));
+    misc[2] = 0;
+    misc[3] = 0;
   }
   __syncthreads();
 }
@@ -174,50 +189,50 @@ __device__ __forceinline__ void walk_init(const DecodeArgs& a, const int* misc, 
     w.t1 = static_cast<int>(min(t0 + w.R, static_cast<int64_t>(total)));
   } else {
     w.item = blockIdx.x;
-    w.items = a.batch * a.num_kv_heads * a.splits;
+    w.items = a.batch * a.units * a.splits;
   }
 }
 
 __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const int* lens, const int* prefix, Walk& w,
                                           Seg& s) {
-  const int H = a.num_kv_heads;
+  const int U = a.units;
   if (a.splits == 0) {
     if (w.t >= w.t1) return false;
-    int lo = 0, hi = a.batch - 1;  // largest b with H * prefix[b] <= t
+    int lo = 0, hi = a.batch - 1;  // largest b with U * prefix[b] <= t
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (static_cast<int64_t>(H) * prefix[mid] <= w.t) lo = mid; else hi = mid - 1;
+      if (static_cast<int64_t>(U) * prefix[mid] <= w.t) lo = mid; else hi = mid - 1;
     }
     const int b = lo;
     const int n = prefix[b + 1] - prefix[b];
-    const int seq0 = H * prefix[b];
+    const int seq0 = U * prefix[b];
     const int off = w.t - seq0;
-    const int kvh = off / n, tile = off - kvh * n;
+    const int u = off / n, tile = off - u * n;
     const int len = min(n - tile, w.t1 - w.t);
-    const int s_begin = seq0 + kvh * n;
+    const int s_begin = seq0 + u * n;
     const int s_end = s_begin + n;
     s.b = b;
-    s.kvh = kvh;
+    s.u = u;
     s.tok_begin = tile * kTile;
     s.tok_end = min(lens[b], (tile + len) * kTile);
     s.c_first = s_begin / w.R;
     s.nchunks = (s_end - 1) / w.R - s.c_first + 1;
     s.first_aligned = s_begin == s.c_first * w.R;
     s.whole = s.nchunks == 1;
-    s.slot = w.t == static_cast<int>(blockIdx.x) * w.R ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+    s.chunk = w.t == static_cast<int>(blockIdx.x) * w.R ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
     w.t += len;
     return true;
   }
   if (w.item >= w.items) return false;
   const int i = w.item;
   const int S = a.splits;
-  s.kvh = i % H;
-  const int sp = (i / H) % S;
-  s.b = i / (H * S);
+  s.u = i % U;
+  const int sp = (i / U) % S;
+  s.b = i / (U * S);
   const int span = a.pages_per_split * a.page_size;
   s.tok_begin = sp * span;
   s.tok_end = max(s.tok_begin, min(lens[s.b], s.tok_begin + span));
-  s.slot = i;
+  s.chunk = i;
   s.nchunks = S;
   s.c_first = 0;
   s.first_aligned = true;
@@ -226,75 +241,20 @@ __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const int* lens, 
   return true;
 }
 
-__device__ __forceinline__ int chunk_slot(const DecodeArgs& a, const Seg& s, int k) {
+// Chunk id of the k-th chunk of segment s's (sequence, unit).
+__device__ __forceinline__ int chunk_id(const DecodeArgs& a, const Seg& s, int k) {
   if (a.splits == 0) {
     const int c = s.c_first + k;
     return (k == 0 && !s.first_aligned) ? 2 * c + 1 : 2 * c;
   }
-  return (s.b * a.splits + k) * a.num_kv_heads + s.kvh;
+  return (s.b * a.splits + k) * a.units + s.u;
 }
 
-// ------------------------------------------------------------------------- emit / merge
-
-// One output element of a segment: O / L is the normalised value, M (base 2) its max.
-template <typename T>
-__device__ __forceinline__ void emit_value(const DecodeArgs& a, const Seg& s, int h, int d, float O, float L,
-                                           float M) {
-  const int G = a.group, D = a.head_dim;
-  const float o = L > 0.0f ? O / L : 0.0f;
-  if (s.whole) {
-    T* out = static_cast<T*>(a.out);
-    out[(static_cast<int64_t>(s.b) * a.num_q_heads + s.kvh * G + h) * D + d] = Storage<T>::store(o);
-  } else {
-    a.part_o[(static_cast<int64_t>(s.slot) * G + h) * D + d] = o;
-    if (d == 0) a.part_lse[static_cast<int64_t>(s.slot) * G + h] = L > 0.0f ? M + __log2f(L) : -INFINITY;
-  }
+__device__ __forceinline__ uint32_t* counter_of(const DecodeArgs& a, int b, int kvh, int hg) {
+  return a.sync + 1 + (static_cast<int64_t>(b) * a.num_kv_heads + kvh) * kMaxHeadGroups + hg;
 }
 
-// Called by the `nthr` threads that emitted this segment. The chunk's partial is
-// published; the last chunk to arrive for its (sequence, KV head) merges them all.
-template <typename T, typename Sync>
-__device__ __forceinline__ void merge_if_last(const DecodeArgs& a, const Seg& s, int ctid, int nthr,
-                                              volatile int* flag, Sync sync) {
-  if (s.whole) return;
-  __threadfence();
-  sync();
-  uint32_t* counter = a.sync + 1 + s.b * a.num_kv_heads + s.kvh;
-  if (ctid == 0) {
-    const uint32_t old = atomicAdd(counter, 1u);
-    *flag = old == static_cast<uint32_t>(s.nchunks - 1);
-  }
-  sync();
-  if (*flag) {
-    __threadfence();
-    const int G = a.group, D = a.head_dim;
-    T* out = static_cast<T*>(a.out);
-    for (int idx = ctid; idx < G * D; idx += nthr) {
-      const int h = idx / D, d = idx - h * D;
-      float M = -INFINITY;
-      for (int k = 0; k < s.nchunks; ++k) {
-        M = fmaxf(M, __ldcg(a.part_lse + static_cast<int64_t>(chunk_slot(a, s, k)) * G + h));
-      }
-      float W = 0.0f, O = 0.0f;
-      if (M > -INFINITY) {
-        for (int k = 0; k < s.nchunks; ++k) {
-          const int64_t slot = chunk_slot(a, s, k);
-          const float lse = __ldcg(a.part_lse + slot * G + h);
-          if (lse > -INFINITY) {
-            const float wk = fast_exp2(lse - M);
-            W += wk;
-            O += wk * __ldcg(a.part_o + (slot * G + h) * D + d);
-          }
-        }
-      }
-      out[(static_cast<int64_t>(s.b) * a.num_q_heads + s.kvh * G + h) * D + d] =
-          Storage<T>::store(W > 0.0f ? O / W : 0.0f);
-    }
-    if (ctid == 0) atomicExch(counter, 0u);
-  }
-}
-
-// Zero the outputs of empty sequences (balanced mode has no work item for them).
+// Zero the outputs of empty sequences (balanced mode has no work for them).
 template <typename T>
 __device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const int* lens, int ctid, int nthr) {
   if (a.splits != 0) return;
@@ -309,25 +269,28 @@ __device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const 
 // ------------------------------------------------------------------------- tensor-core kernel
 
 struct TcLayout {
-  uint32_t stage_bytes, ring, bars, red_m, red_l, red_acc, misc, prefix, lens, total;
+  uint32_t head_bytes, half, stage_bytes, ring, bars, red_m, red_l, red_acc, misc, prefix, lens, total;
 };
 
 __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline TcLayout tc_layout(int D, int NT, int nstage, int batch) {
+__host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int nstage, int batch) {
   TcLayout L{};
-  L.stage_bytes = 2u * kTile * D * 2u;
+  L.head_bytes = kTile * D * 2u;  // one head's K (or V) rows of a tile: D/64 swizzled 2 KB chunks
+  L.half = HT * L.head_bytes;
+  L.stage_bytes = 2u * L.half;
   uint32_t off = 0;
   L.ring = off;
   off += nstage * L.stage_bytes;
   L.bars = off;
   off += 2u * nstage * 8u;
+  const uint32_t red_warps = TW > 1 ? kCW : 0;
   L.red_m = off;
-  off += kCW * 8u * NT * 4u;
+  off += red_warps * 8u * NT * 4u;
   L.red_l = off;
-  off += kCW * 8u * NT * 4u;
+  off += red_warps * 8u * NT * 4u;
   L.red_acc = off;
-  off += kCW * 8u * NT * (D + 4u) * 4u;
+  off += red_warps * 8u * NT * (D + 4u) * 4u;
   L.misc = off;
   off += 64u * 4u;
   L.prefix = off;
@@ -339,19 +302,18 @@ __host__ __device__ inline TcLayout tc_layout(int D, int NT, int nstage, int bat
 }
 
 template <typename T, int D, int NT>
-__global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_constant__ CUtensorMap tmk,
-                                                               const __grid_constant__ CUtensorMap tmv,
-                                                               const DecodeArgs a, const int nstage,
-                                                               const int p_rows, const int hg_count) {
+__global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap tmk,
+                                                                  const __grid_constant__ CUtensorMap tmv,
+                                                                  const DecodeArgs a, const TcShape cfg) {
   constexpr int KS = D / 16;   // k-steps of K.Q^T, m-tiles of V^T.P^T
   constexpr int NCH = D / 64;  // 128-byte chunks of one token row of one head
   constexpr int HPW = 8 * NT;  // query heads per consumer warp
-  constexpr uint32_t kHalf = kTile * D * 2;  // bytes of the K (or V) half of a stage
   constexpr uint32_t kChunkBytes = kTile * 128;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const TcLayout L = tc_layout(D, NT, nstage, a.batch);
+  const int HT = cfg.ht, HG = cfg.hg, TW = cfg.tw, nstage = cfg.nstage;
+  const TcLayout L = tc_layout(D, NT, HT, TW, nstage, a.batch);
   const uint32_t ring = smem_u32(smem + L.ring);
   const uint32_t bars = smem_u32(smem + L.bars);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m);
@@ -362,12 +324,11 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
   int* lens = reinterpret_cast<int*>(smem + L.lens);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int HG = hg_count, TW = kCW / hg_count;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < nstage; ++s) {
       mbar_init(bars + 8u * s, 1);                    // full: the producer's expect_tx arrival
-      mbar_init(bars + 8u * (nstage + s), hg_count);  // empty: one arrival per consuming warp
+      mbar_init(bars + 8u * (nstage + s), HT * HG);   // empty: every warp that reads the stage
     }
     fence_barrier_init();
   }
@@ -379,14 +340,16 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
   volatile int* abort_flag = misc + 2;
 
   if (warp == kCW) {
-    // ---------------- producer warp
+    // ---------------- producer warp: one tile (all HT heads, K and V) per stage
     Walk w;
     walk_init(a, misc, w);
     Seg s;
     uint32_t gt = 0;
     const uint64_t policy = l2_policy_evict_first();
+    const int p_rows = cfg.p_rows;
     const int nsub = kTile / p_rows;
-    const uint32_t sub_bytes = 2u * NCH * p_rows * 128u;
+    const int n_tma = 2 * HT * NCH * nsub;
+    const uint32_t sub_bytes = 2u * HT * NCH * p_rows * 128u;
     bool ok = true;
     while (ok && walk_next(a, lens, prefix, w, s)) {
       const int ntok = s.tok_end - s.tok_begin;
@@ -394,8 +357,8 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
       const int ntiles = (ntok + kTile - 1) / kTile;
       const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.b) * a.bt_stride;
       const int last_page = (s.tok_end - 1) / a.page_size;
-      // The warp caches 32 consecutive block-table entries (one per lane) and
-      // prefetches the next 32, so page lookups never stall the TMA issue.
+      const int x0 = s.u * HT * D;
+      // 32 consecutive block-table entries cached one per lane, the next 32 prefetched.
       int cur_base = INT_MIN / 2, nxt_base = INT_MIN / 2;
       int32_t cur = 0, nxt = 0;
       for (int j = 0; j < ntiles; ++j, ++gt) {
@@ -408,14 +371,12 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
           break;
         }
         const int t0 = s.tok_begin + j * kTile;
-        uint32_t bytes = 0;
-        int ys[2] = {0, 0};
-        bool vs[2] = {false, false};
+        bool v0 = false, v1 = false;
+        int y0 = 0, y1 = 0;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          if (r >= nsub) break;
           const int tok = t0 + r * p_rows;
-          if (tok >= s.tok_end) break;
+          if (r >= nsub || tok >= s.tok_end) break;
           const int pidx = tok / a.page_size;
           if (pidx < cur_base || pidx >= cur_base + 32) {
             if (pidx == nxt_base) {
@@ -429,29 +390,31 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
             nxt = nxt_base + lane <= last_page ? __ldg(bt_row + nxt_base + lane) : 0;
           }
           const int page = __shfl_sync(0xffffffffu, cur, pidx - cur_base);
-          if (page < 0 || (a.num_pages >= 0 && page >= a.num_pages)) {
-            if (lane == 0) atomicOr(a.sync, kStatusBadPage);
+          const bool good = page >= 0 && (a.num_pages < 0 || page < a.num_pages);
+          if (!good && lane == 0) atomicOr(a.sync, kStatusBadPage);
+          const int y = good ? page * a.page_size + (tok - pidx * a.page_size) : 0;
+          if (r == 0) {
+            v0 = good;
+            y0 = y;
           } else {
-            vs[r] = true;
-            ys[r] = page * a.page_size + (tok - pidx * a.page_size);
-            bytes += sub_bytes;
+            v1 = good;
+            y1 = y;
           }
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(full, bytes);
-          const uint32_t sk = ring + stage * L.stage_bytes;
-          const uint32_t sv = sk + kHalf;
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            if (!vs[r]) continue;
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-              const uint32_t dst = c * kChunkBytes + r * p_rows * 128u;
-              const int x = s.kvh * D + c * 64;
-              tma_load_2d(sk + dst, &tmk, x, ys[r], full, policy);
-              tma_load_2d(sv + dst, &tmv, x, ys[r], full, policy);
-            }
-          }
+        if (lane == 0) mbar_arrive_expect_tx(full, (v0 ? sub_bytes : 0u) + (v1 ? sub_bytes : 0u));
+        __syncwarp();
+        const uint32_t sbase = ring + stage * L.stage_bytes;
+        for (int idx = lane; idx < n_tma; idx += 32) {
+          const int r = idx % nsub;
+          int rest = idx / nsub;
+          const int c = rest % NCH;
+          rest /= NCH;
+          const int ht = rest % HT;
+          const int tensor = rest / HT;
+          if (!(r ? v1 : v0)) continue;
+          const uint32_t dst = sbase + tensor * L.half + ht * L.head_bytes + c * kChunkBytes + r * p_rows * 128u;
+          tma_load_2d(dst, tensor ? static_cast<const void*>(&tmv) : static_cast<const void*>(&tmk),
+                      x0 + ht * D + c * 64, r ? y1 : y0, full, policy);
         }
         __syncwarp();
       }
@@ -464,10 +427,12 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
     return;
   }
 
-  // ---------------- consumer warps (threads 0..127)
-  const int ctid = threadIdx.x;
-  zero_empty_sequences<T>(a, lens, ctid, kCW * 32);
-  const int hg = warp % HG, tw = warp / HG;
+  // ---------------- consumer warps (threads 0..255)
+  zero_empty_sequences<T>(a, lens, threadIdx.x, kCW * 32);
+  const int ht = warp % HT;
+  const int hg = (warp / HT) % HG;
+  const int tw = warp / (HT * HG);
+  const int mu = ht * HG + hg;  // (head, group) within the unit: slot and barrier index
   const int g = lane >> 2, t4 = lane & 3;
   const int mi = lane >> 3, r8 = lane & 7;
   // ldmatrix row addresses: K (A operand of S = K.Q^T) and V (A operand of O^T = V^T.P^T, transposed).
@@ -476,7 +441,7 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
   const uint32_t v_row = (r8 + 8 * (mi >> 1)) * 128u;
   const int v_half = mi & 1;
   const float sl = a.scale_log2;
-  const auto csync = [] { named_barrier(1, kCW * 32); };
+  const int G = a.group;
 
   Walk w;
   walk_init(a, misc, w);
@@ -485,14 +450,15 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
   while (walk_next(a, lens, prefix, w, s)) {
     const int ntok = max(0, s.tok_end - s.tok_begin);
     const int ntiles = (ntok + kTile - 1) / kTile;
+    const int kvh = s.u * HT + ht;
 
     // Q^T as the B operand: lane holds q[head g][2t4, 2t4+1] and [2t4+8, 2t4+9] of each k-step.
     uint32_t qf[KS][NT][2];
-    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + s.kvh * a.group) * D;
+    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int h = hg * HPW + nt * 8 + g;
-      const bool hv = h < a.group;
+      const bool hv = h < G;
       const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qb + static_cast<int64_t>(hv ? h : 0) * D);
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
@@ -519,8 +485,8 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
         break;
       }
       const int valid = min(kTile, ntok - j * kTile);
-      const uint32_t sk = ring + stage * L.stage_bytes;
-      const uint32_t sv = sk + kHalf;
+      const uint32_t sk = ring + stage * L.stage_bytes + ht * L.head_bytes;
+      const uint32_t sv = sk + L.half;
 
       // S = K . Q^T : [16 tokens x 8 heads] per n-tile.
       float sc[NT][4];
@@ -597,7 +563,7 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
     }
     gt += ntiles;
 
-    // Publish this warp's (m, l, acc) and combine the tile-parallel warps of each head group.
+    // Per-head normaliser over the 8 token-row groups of the fragments.
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -609,47 +575,149 @@ __global__ void __launch_bounds__(kTCThreads) decode_tc_kernel(const __grid_cons
         l_run[nt][e] = l;
       }
     }
-    float* rm = red_m + warp * HPW;
-    float* rl = red_l + warp * HPW;
-    float* ra = red_acc + warp * HPW * (D + 4);
+
+    // Warps that split the tiles of one (head, group) combine into the tw == 0 warp.
+    if (TW > 1) {
+      if (tw != 0) {
+        float* rm = red_m + warp * HPW;
+        float* rl = red_l + warp * HPW;
+        float* ra = red_acc + warp * HPW * (D + 4);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int hl = nt * 8 + 2 * t4 + e;
+            if (g == 0) {
+              rm[hl] = m_run[nt][e];
+              rl[hl] = l_run[nt][e];
+            }
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+              ra[hl * (D + 4) + mt * 16 + g] = acc[mt][nt][e];
+              ra[hl * (D + 4) + mt * 16 + g + 8] = acc[mt][nt][2 + e];
+            }
+          }
+        }
+      }
+      named_barrier(1 + mu, TW * 32);
+      if (tw == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int hl = nt * 8 + 2 * t4 + e;
+            float M = m_run[nt][e];
+            for (int t2 = 1; t2 < TW; ++t2) M = fmaxf(M, red_m[(mu + HT * HG * t2) * HPW + hl]);
+            if (M == -INFINITY) continue;
+            const float f0 = fast_exp2(m_run[nt][e] - M);
+            float l = l_run[nt][e] * f0;
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+              acc[mt][nt][e] *= f0;
+              acc[mt][nt][2 + e] *= f0;
+            }
+            for (int t2 = 1; t2 < TW; ++t2) {
+              const int w2 = mu + HT * HG * t2;
+              const float m2 = red_m[w2 * HPW + hl];
+              if (m2 == -INFINITY) continue;
+              const float f = fast_exp2(m2 - M);
+              l += red_l[w2 * HPW + hl] * f;
+              const float* ra = red_acc + (w2 * HPW + hl) * (D + 4);
+#pragma unroll
+              for (int mt = 0; mt < KS; ++mt) {
+                acc[mt][nt][e] += ra[mt * 16 + g] * f;
+                acc[mt][nt][2 + e] += ra[mt * 16 + g + 8] * f;
+              }
+            }
+            m_run[nt][e] = M;
+            l_run[nt][e] = l;
+          }
+        }
+      }
+      named_barrier(1 + mu, TW * 32);
+      if (tw != 0) continue;
+    }
+
+    // ---- emit: the final output, or this chunk's partial and (if last) the merge.
+    T* out = static_cast<T*>(a.out);
+    const int64_t out_row0 = static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G + hg * HPW;
+    if (s.whole) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int hl = nt * 8 + 2 * t4 + e;
+          if (hg * HPW + hl >= G) continue;
+          const float inv = l_run[nt][e] > 0.0f ? 1.0f / l_run[nt][e] : 0.0f;
+          T* orow = out + (out_row0 + hl) * D;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            orow[mt * 16 + g] = Storage<T>::store(acc[mt][nt][e] * inv);
+            orow[mt * 16 + g + 8] = Storage<T>::store(acc[mt][nt][2 + e] * inv);
+          }
+        }
+      }
+      continue;
+    }
+    const int64_t slot = static_cast<int64_t>(s.chunk) * (HT * HG) + mu;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int hl = nt * 8 + 2 * t4 + e;
-        if (g == 0) {
-          rm[hl] = m_run[nt][e];
-          rl[hl] = l_run[nt][e];
-        }
+        const float l = l_run[nt][e];
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        float* po = a.part_o + (slot * HPW + hl) * D;
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-          ra[hl * (D + 4) + mt * 16 + g] = acc[mt][nt][e];
-          ra[hl * (D + 4) + mt * 16 + g + 8] = acc[mt][nt][2 + e];
+          po[mt * 16 + g] = acc[mt][nt][e] * inv;
+          po[mt * 16 + g + 8] = acc[mt][nt][2 + e] * inv;
         }
+        if (g == 0) a.part_lse[slot * HPW + hl] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
       }
     }
-    csync();
-    for (int idx = ctid; idx < a.group * D; idx += kCW * 32) {
-      const int h = idx / D, d = idx - h * D;
-      const int hgi = h / HPW, hl = h - hgi * HPW;
-      float M = -INFINITY;
-      for (int tw2 = 0; tw2 < TW; ++tw2) M = fmaxf(M, red_m[(tw2 * HG + hgi) * HPW + hl]);
-      float O = 0.0f, Ls = 0.0f;
-      if (M > -INFINITY) {
-        for (int tw2 = 0; tw2 < TW; ++tw2) {
-          const int wi = tw2 * HG + hgi;
-          const float mw = red_m[wi * HPW + hl];
-          if (mw > -INFINITY) {
-            const float f = fast_exp2(mw - M);
-            Ls += red_l[wi * HPW + hl] * f;
-            O += red_acc[(wi * HPW + hl) * (D + 4) + d] * f;
+    __threadfence();
+    __syncwarp();
+    uint32_t* counter = counter_of(a, s.b, kvh, hg);
+    int last = 0;
+    if (lane == 0) last = atomicAdd(counter, 1u) == static_cast<uint32_t>(s.nchunks - 1);
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      const int nh = min(HPW, G - hg * HPW);
+      for (int i = lane; i < nh * (D / 4); i += 32) {
+        const int hl = i / (D / 4);
+        const int d4 = (i - hl * (D / 4)) * 4;
+        float M = -INFINITY;
+        for (int k = 0; k < s.nchunks; ++k) {
+          const int64_t sk2 = static_cast<int64_t>(chunk_id(a, s, k)) * (HT * HG) + mu;
+          M = fmaxf(M, __ldcg(a.part_lse + sk2 * HPW + hl));
+        }
+        float W = 0.0f;
+        float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (M > -INFINITY) {
+          for (int k = 0; k < s.nchunks; ++k) {
+            const int64_t sk2 = static_cast<int64_t>(chunk_id(a, s, k)) * (HT * HG) + mu;
+            const float lse = __ldcg(a.part_lse + sk2 * HPW + hl);
+            if (lse == -INFINITY) continue;
+            const float f = fast_exp2(lse - M);
+            const float4 o = __ldcg(reinterpret_cast<const float4*>(a.part_o + (sk2 * HPW + hl) * D + d4));
+            W += f;
+            O.x += f * o.x;
+            O.y += f * o.y;
+            O.z += f * o.z;
+            O.w += f * o.w;
           }
         }
+        const float inv = W > 0.0f ? 1.0f / W : 0.0f;
+        T* orow = out + (out_row0 + hl) * D + d4;
+        orow[0] = Storage<T>::store(O.x * inv);
+        orow[1] = Storage<T>::store(O.y * inv);
+        orow[2] = Storage<T>::store(O.z * inv);
+        orow[3] = Storage<T>::store(O.w * inv);
       }
-      emit_value<T>(a, s, h, d, O, Ls, M);
+      if (lane == 0) atomicExch(counter, 0u);
     }
-    merge_if_last<T>(a, s, ctid, kCW * 32, misc + 3, csync);
-    csync();
   }
 }
 
@@ -687,6 +755,7 @@ __host__ __device__ inline GenLayout gen_layout(int G, int D, int batch) {
   return L;
 }
 
+// One CTA of 128 threads handles one (sequence, KV head) chunk at a time.
 template <typename T>
 __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const DecodeArgs a) {
   extern __shared__ __align__(16) uint8_t gsmem[];
@@ -706,14 +775,15 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
 
   plan_build(a, lens, prefix, misc);
   zero_empty_sequences<T>(a, lens, tid, kGenThreads);
-  const auto bsync = [] { __syncthreads(); };
   const int64_t tok_stride = static_cast<int64_t>(H) * D;
+  T* out = static_cast<T*>(a.out);
 
   Walk w;
   walk_init(a, misc, w);
   Seg s;
   while (walk_next(a, lens, prefix, w, s)) {
-    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + s.kvh * G) * D;
+    const int kvh = s.u;
+    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
     for (int i = tid; i < G * D; i += kGenThreads) {
       q_s[i] = Storage<T>::load(qb[i]);
       acc_s[i] = 0.0f;
@@ -722,8 +792,8 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
       m_s[tid] = -INFINITY;
       l_s[tid] = 0.0f;
     }
-    const T* kc = static_cast<const T*>(a.k_cache) + s.kvh * D;
-    const T* vc = static_cast<const T*>(a.v_cache) + s.kvh * D;
+    const T* kc = static_cast<const T*>(a.k_cache) + kvh * D;
+    const T* vc = static_cast<const T*>(a.v_cache) + kvh * D;
     const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.b) * a.bt_stride;
     __syncthreads();
     for (int base = s.tok_begin; base < s.tok_end; base += kGenChunk) {
@@ -786,11 +856,52 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
       }
       __syncthreads();
     }
+
+    const int64_t out_row0 = static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G;
+    if (s.whole) {
+      for (int idx = tid; idx < G * D; idx += kGenThreads) {
+        const int h = idx / D;
+        const float l = l_s[h];
+        out[out_row0 * D + idx] = Storage<T>::store(l > 0.0f ? acc_s[idx] / l : 0.0f);
+      }
+      __syncthreads();
+      continue;
+    }
+    const int64_t slot = s.chunk;
     for (int idx = tid; idx < G * D; idx += kGenThreads) {
       const int h = idx / D, d = idx - h * D;
-      emit_value<T>(a, s, h, d, acc_s[idx], l_s[h], m_s[h]);
+      const float l = l_s[h];
+      a.part_o[(slot * G + h) * D + d] = l > 0.0f ? acc_s[idx] / l : 0.0f;
+      if (d == 0) a.part_lse[slot * G + h] = l > 0.0f ? m_s[h] + __log2f(l) : -INFINITY;
     }
-    merge_if_last<T>(a, s, tid, kGenThreads, misc + 3, bsync);
+    __threadfence();
+    __syncthreads();
+    uint32_t* counter = counter_of(a, s.b, kvh, 0);
+    if (tid == 0) misc[3] = atomicAdd(counter, 1u) == static_cast<uint32_t>(s.nchunks - 1);
+    __syncthreads();
+    if (misc[3]) {
+      __threadfence();
+      for (int idx = tid; idx < G * D; idx += kGenThreads) {
+        const int h = idx / D, d = idx - h * D;
+        float M = -INFINITY;
+        for (int k = 0; k < s.nchunks; ++k) {
+          M = fmaxf(M, __ldcg(a.part_lse + static_cast<int64_t>(chunk_id(a, s, k)) * G + h));
+        }
+        float W = 0.0f, O = 0.0f;
+        if (M > -INFINITY) {
+          for (int k = 0; k < s.nchunks; ++k) {
+            const int64_t sk2 = chunk_id(a, s, k);
+            const float lse = __ldcg(a.part_lse + sk2 * G + h);
+            if (lse == -INFINITY) continue;
+            const float f = fast_exp2(lse - M);
+            W += f;
+            O += f * __ldcg(a.part_o + (sk2 * G + h) * D + d);
+          }
+        }
+        out[out_row0 * D + idx] = Storage<T>::store(W > 0.0f ? O / W : 0.0f);
+      }
+      if (tid == 0) atomicExch(counter, 0u);
+    }
     __syncthreads();
   }
 }
@@ -801,11 +912,13 @@ namespace {
 
 struct Plan {
   bool tc = false;
-  int D = 0, NT = 1, HG = 1, nstage = 0, p_rows = 16;
+  int D = 0, NT = 1;
+  TcShape shape{};
   size_t smem = 0;
   int grid = 0;
+  int units = 0;
   int splits = 0, pps = 0;
-  int slots = 0;
+  int slots = 0, slot_heads = 0;
   size_t part_bytes = 0, sync_bytes = 0;
   const void* fn = nullptr;
 };
@@ -824,8 +937,8 @@ int device_sms(int dev) {
   return cache[dev];
 }
 
-// Blocks per SM for `fn` at `smem` dynamic bytes; also raises the kernel's
-// dynamic shared-memory limit on first use on this device.
+// Blocks per SM for `fn` at `smem` dynamic bytes; also raises the kernel's dynamic
+// shared-memory limit on first use on this device.
 int blocks_per_sm(int dev, const void* fn, int threads, size_t smem) {
   static std::map<std::tuple<int, const void*, size_t>, int> occ;
   static std::map<std::pair<int, const void*>, bool> attr;
@@ -861,11 +974,19 @@ const void* gen_fn(int dtype) {
 }
 
 constexpr int kMinTilesPerCta = 4;
-constexpr uint32_t kSmemTarget = 112 * 1024;  // two CTAs per SM
+constexpr uint32_t kTcSmemBudget = 200 * 1024;  // one tensor-core CTA per SM
+constexpr int kMaxStages = 24;
 
-// Partial outputs [slots][G][D] fp32 first, then their LSEs [slots][G], 256-byte aligned.
-size_t lse_offset(int slots, int G, int D) {
-  return (static_cast<size_t>(slots) * G * D * 4 + 255) / 256 * 256;
+// Optional tuning overrides read once from the environment:
+//   KL_DECODE_HEADS_PER_TILE (1/2/4/8), KL_DECODE_STAGES (2..24). 0 = automatic.
+int env_int(const char* name) {
+  const char* v = std::getenv(name);
+  return v ? std::atoi(v) : 0;
+}
+
+// Partial outputs [slots][slot_heads][D] fp32 first, then their LSEs, 256-byte aligned.
+size_t lse_offset(int slots, int slot_heads, int D) {
+  return (static_cast<size_t>(slots) * slot_heads * D * 4 + 255) / 256 * 256;
 }
 
 // Launch shape and scratch sizes of one decode call. `generic` forces the CUDA-core kernel.
@@ -879,35 +1000,60 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   const int G = Hq / Hkv;
   const int64_t max_tokens = static_cast<int64_t>(max_pages) * P;
   if (max_tokens > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
-  const int64_t total_tiles = static_cast<int64_t>(batch) * ((max_tokens + kTile - 1) / kTile) * Hkv;
-  if (total_tiles > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
+  const int64_t max_tiles = (max_tokens + kTile - 1) / kTile;
+  if (static_cast<int64_t>(batch) * max_tiles * Hkv > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return static_cast<int>(cudaErrorNoDevice);
   const int sms = device_sms(dev);
   if (sms <= 0) return static_cast<int>(cudaErrorNoDevice);
 
   p.D = D;
+  const int NT = (G > 8 && D <= 128) ? 2 : 1;
+  const int hg_need = (G + 8 * NT - 1) / (8 * NT);
+  const int HG = hg_need <= 1 ? 1 : hg_need <= 2 ? 2 : hg_need <= 4 ? 4 : 0;
   p.tc = !generic && dtype != KL_FLOAT32 && (D == 64 || D == 128 || D == 256) && (P == 8 || P % 16 == 0) &&
-         (D == 256 ? G <= 32 : G <= 64);
+         HG > 0;
   int threads;
   if (p.tc) {
-    p.NT = (G > 8 && D <= 128) ? 2 : 1;
-    const int need = (G + 8 * p.NT - 1) / (8 * p.NT);
-    p.HG = need <= 1 ? 1 : need <= 2 ? 2 : 4;
-    p.p_rows = P < 16 ? P : 16;
-    const TcLayout base = tc_layout(D, p.NT, 0, batch);
-    const uint32_t stage = 2u * kTile * D * 2u + 16u;
-    int ns = base.total < kSmemTarget ? static_cast<int>((kSmemTarget - base.total) / stage) : 0;
-    ns = std::min(16, ns);
-    if (ns < 4) ns = 4;  // one CTA per SM then
-    p.nstage = ns;
-    p.smem = tc_layout(D, p.NT, ns, batch).total;
-    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, p.NT) : tc_fn<__nv_bfloat16>(D, p.NT);
+    p.NT = NT;
+    // Heads per tile: a power of two dividing Hkv, at most 8 / HG warps' worth, a stage of
+    // at most 64 KB, and enough (sequence, head-block) tiles to keep every SM busy.
+    int ht = 1;
+    while (ht * 2 <= 8 / HG && Hkv % (ht * 2) == 0 && ht * 2 * D <= 1024) ht *= 2;
+    while (ht > 1 && static_cast<int64_t>(batch) * max_tiles * (Hkv / ht) < 4LL * sms) ht /= 2;
+    const int forced_ht = env_int("KL_DECODE_HEADS_PER_TILE");
+    if (forced_ht > 0 && forced_ht <= 8 / HG && Hkv % forced_ht == 0 && (forced_ht & (forced_ht - 1)) == 0 &&
+        forced_ht * D <= 1024) {
+      ht = forced_ht;
+    }
+    p.shape.ht = ht;
+    p.shape.hg = HG;
+    p.shape.tw = kCW / (ht * HG);
+    p.shape.p_rows = P < 16 ? P : 16;
+    const TcLayout base = tc_layout(D, NT, ht, p.shape.tw, 0, batch);
+    const uint32_t stage = base.stage_bytes + 16u;
+    int ns = base.total < kTcSmemBudget ? static_cast<int>((kTcSmemBudget - base.total) / stage) : 0;
+    ns = std::min(kMaxStages, ns);
+    const int forced_ns = env_int("KL_DECODE_STAGES");
+    if (forced_ns >= 2) ns = std::min(ns, forced_ns);
+    // Stage s is consumed only by the warps with tw == s % TW, in order, so a warp never
+    // waits on a stage whose previous phase belongs to another warp: with a stage count
+    // that is not a multiple of TW, a wait for phase k could be satisfied by phase k-2
+    // (same parity) and the ring would fall out of step.
+    ns = ns / p.shape.tw * p.shape.tw;
+    if (ns < std::max(2, p.shape.tw)) return static_cast<int>(cudaErrorInvalidValue);
+    p.shape.nstage = ns;
+    p.smem = tc_layout(D, NT, ht, p.shape.tw, ns, batch).total;
+    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, NT) : tc_fn<__nv_bfloat16>(D, NT);
+    p.units = Hkv / ht;
+    p.slot_heads = 8 * NT;
     threads = kTCThreads;
   } else {
     if (static_cast<int64_t>(G) * D > 8192) return static_cast<int>(cudaErrorInvalidValue);
     p.smem = gen_layout(G, D, batch).total;
     p.fn = gen_fn(dtype);
+    p.units = Hkv;
+    p.slot_heads = G;
     threads = kGenThreads;
   }
   int max_optin = 0;
@@ -916,21 +1062,23 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   const int per_sm = blocks_per_sm(dev, p.fn, threads, p.smem);
   if (per_sm <= 0) return static_cast<int>(cudaErrorInvalidConfiguration);
 
+  const int slots_per_chunk = p.tc ? p.shape.ht * p.shape.hg : 1;
+  int64_t chunks;
   if (num_splits > 0) {
     const int mp = std::max(1, max_pages);
     p.pps = (mp + num_splits - 1) / num_splits;
     p.splits = (mp + p.pps - 1) / p.pps;
-    const int64_t items = static_cast<int64_t>(batch) * Hkv * p.splits;
-    if (items > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
-    p.slots = static_cast<int>(items);
-    p.grid = static_cast<int>(std::min<int64_t>(items, static_cast<int64_t>(sms) * per_sm));
+    chunks = static_cast<int64_t>(batch) * p.units * p.splits;
+    p.grid = static_cast<int>(std::min<int64_t>(chunks, static_cast<int64_t>(sms) * per_sm));
   } else {
     p.splits = 0;
     p.grid = sms * per_sm;
-    p.slots = 2 * p.grid;
+    chunks = 2LL * p.grid;
   }
-  p.part_bytes = lse_offset(p.slots, G, D) + static_cast<size_t>(p.slots) * G * 4;
-  p.sync_bytes = (1 + static_cast<size_t>(batch) * Hkv) * 4;
+  if (chunks * slots_per_chunk > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
+  p.slots = static_cast<int>(chunks * slots_per_chunk);
+  p.part_bytes = lse_offset(p.slots, p.slot_heads, D) + static_cast<size_t>(p.slots) * p.slot_heads * 4;
+  p.sync_bytes = (1 + static_cast<size_t>(batch) * Hkv * kMaxHeadGroups) * 4;
   return 0;
 }
 
@@ -972,18 +1120,17 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 template <typename T>
 cudaError_t launch_tc(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                       cudaStream_t st) {
-  const int hg = p.HG;
   switch (p.D) {
     case 64:
-      if (p.NT == 1) decode_tc_kernel<T, 64, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.nstage, p.p_rows, hg);
-      else decode_tc_kernel<T, 64, 2><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.nstage, p.p_rows, hg);
+      if (p.NT == 1) decode_tc_kernel<T, 64, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+      else decode_tc_kernel<T, 64, 2><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
       break;
     case 128:
-      if (p.NT == 1) decode_tc_kernel<T, 128, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.nstage, p.p_rows, hg);
-      else decode_tc_kernel<T, 128, 2><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.nstage, p.p_rows, hg);
+      if (p.NT == 1) decode_tc_kernel<T, 128, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+      else decode_tc_kernel<T, 128, 2><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
       break;
     default:
-      decode_tc_kernel<T, 256, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.nstage, p.p_rows, hg);
+      decode_tc_kernel<T, 256, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
       break;
   }
   return cudaGetLastError();
@@ -1008,8 +1155,8 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   bool use_tc = false;
   if (tc_ok) {
     const int64_t pool_tokens = num_pages >= 0 ? std::max<int64_t>(num_pages, 1) * P : (int64_t(1) << 31) - 1;
-    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.p_rows) &&
-             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.p_rows);
+    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.p_rows) &&
+             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.p_rows);
   }
   if (!use_tc && p.tc) {
     if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, true, p)) return rc;
@@ -1017,7 +1164,6 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   if (partial_bytes < p.part_bytes || sync_bytes < p.sync_bytes || !partials) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
-  const int G = Hq / Hkv;
   DecodeArgs a{};
   a.out = out;
   a.q = q;
@@ -1028,19 +1174,20 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   a.batch = batch;
   a.num_q_heads = Hq;
   a.num_kv_heads = Hkv;
-  a.group = G;
+  a.group = Hq / Hkv;
   a.head_dim = D;
   a.page_size = P;
   a.bt_stride = bt_stride;
   a.max_pages = max_pages;
   a.num_pages = num_pages;
   a.scale_log2 = scale * 1.4426950408889634f;
+  a.units = p.units;
   a.splits = p.splits;
   a.pages_per_split = p.pps;
   a.min_tiles = kMinTilesPerCta;
   a.sync = static_cast<uint32_t*>(sync);
   a.part_o = static_cast<float*>(partials);
-  a.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + lse_offset(p.slots, G, D));
+  a.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + lse_offset(p.slots, p.slot_heads, D));
 
   if (use_tc) {
     const cudaError_t e = dtype == KL_FLOAT16 ? launch_tc<__half>(p, tmk, tmv, a, st)
@@ -1060,7 +1207,7 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
 
 extern "C" {
 
-const char* kl_version(void) { return "kernel_lab_b200 0.1.0 sm_100a"; }
+const char* kl_version(void) { return "kernel_lab_b200 0.2.0 sm_100a"; }
 
 const char* kl_status_string(int status) {
   return status == 0 ? "success" : cudaGetErrorString(static_cast<cudaError_t>(status));
@@ -1078,7 +1225,7 @@ int kl_paged_decode_workspace_size(int dtype, int batch, int num_q_heads, int nu
                                     max_pages_per_seq, num_splits, false, p)) {
     return rc;
   }
-  // A misaligned call falls back to the generic kernel, whose grid may differ: size for both.
+  // A misaligned call falls back to the generic kernel, whose shape differs: size for both.
   klb::Plan g;
   if (p.tc && klb::make_plan(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq,
                              num_splits, true, g) == 0) {

@@ -10,7 +10,8 @@
 //
 // Rounding follows kernel_lab/reference.py:13-30 exactly:
 //   residual' = T(float(x) + float(residual))          (bit-exact)
-//   out       = T((float(residual') * rstd) * float(w)) with rstd = rsqrt(mean(residual'^2) + eps)
+//   out       = T((float(residual') * rstd) * float(w)) with rstd = 1 / sqrt(mean(residual'^2) + eps)
+//   (IEEE sqrt and division, as the fp32 reference computes it)
 //
 // Rows that are misaligned, of odd width or wider than the register budget use
 // a two-pass fallback that re-reads its own row (from L2) for the output pass.
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_regs(T* __restrict__ out, co
     }
   }
 
-  const float rstd = rsqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
+  const float rstd = 1.0f / sqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
 
 #pragma unroll
   for (int i = 0; i < NPT; ++i) {
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_twopass(T* __restrict__ out,
     }
     ss = fmaf(f, f, ss);
   }
-  const float rstd = rsqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
+  const float rstd = 1.0f / sqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
   const T* src = RES ? rr : xr;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
     orow[i] = Storage<T>::store((Storage<T>::load(src[i]) * rstd) * Storage<T>::load(weight[i]));

@@ -53,6 +53,28 @@ def tolerance(dtype: torch.dtype) -> dict[str, float]:
 
 # The north star's bound: max-abs error vs the fp32-math oracle.
 NORTH_STAR_MAX_ABS = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 2e-2}
+SIGNIFICAND_BITS = {torch.float32: 24, torch.float16: 11, torch.bfloat16: 8}
+
+
+def ulp(dtype: torch.dtype, v: np.ndarray) -> np.ndarray:
+    """Spacing of `dtype` values at |v|."""
+    e = np.floor(np.log2(np.maximum(np.abs(v), 2.0**-126)))
+    return 2.0 ** (e - (SIGNIFICAND_BITS[dtype] - 1))
+
+
+def assert_within_abs_or_ulp(got: torch.Tensor, exact: np.ndarray, dtype: torch.dtype, atol: float | None = None):
+    """|got - exact| <= max(atol, one ulp of dtype at |exact|) everywhere, with `exact` the
+    unrounded fp32 oracle. atol defaults to the north star's bound. Where |exact| is large
+    the two storage values nearest the exact result are more than atol apart, so one ulp
+    is the tightest achievable bound there."""
+    atol = NORTH_STAR_MAX_ABS[dtype] if atol is None else atol
+    g = got.float().cpu().numpy()
+    assert np.isfinite(g).all()
+    err = np.abs(g - exact)
+    bound = np.maximum(atol, ulp(dtype, exact))
+    worst = int(np.argmax(err - bound))
+    assert (err <= bound).all(), f"err {err.flat[worst]} > bound {bound.flat[worst]} at |y|={abs(exact.flat[worst])}"
+    return float(err.max())
 
 
 def sha(t: torch.Tensor) -> str:

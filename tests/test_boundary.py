@@ -121,3 +121,15 @@ def test_cuda_ops_fail_loudly_without_a_device():
     assert not cuda_ops.available()
     with pytest.raises(RuntimeError):
         cuda_ops.rms_norm(torch.randn(2, 8), torch.ones(8))
+
+
+def test_extensions_share_the_process_libstdcxx():
+    """Neither shared object may carry its own copy of libstdc++: a second copy of the
+    iostream/locale state crashes the first TORCH_CHECK that formats a number."""
+    from kernel_lab import capi
+
+    ext = next(capi.LIB_PATH.parent.glob("_C*.so"))
+    for so in (capi.LIB_PATH, ext):
+        nm = subprocess.run(["nm", "-C", "--defined-only", str(so)], capture_output=True, text=True, check=True)
+        bad = re.findall(r" [TW] (std::(?:codecvt|basic_ostream|locale)\S*)", nm.stdout)
+        assert not bad, f"{so.name} defines libstdc++ internals: {bad[:3]}"
