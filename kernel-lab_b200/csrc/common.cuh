@@ -2,9 +2,9 @@
 // reductions, and thin inline-PTX wrappers for mbarriers, TMA tensor loads,
 // ldmatrix / movmatrix and the m16n8k16 tensor-core MMA.
 //
-// Every wait on an mbarrier is bounded by wall time (the %globaltimer register):
-// a wait that runs out records an error bit in the caller's status word and
-// returns false, so a kernel can stop cleanly instead of hanging the GPU.
+// Every wait on an mbarrier is bounded (by the SM cycle counter): a wait that runs
+// out records an error bit in the caller's status word and returns false, so a
+// kernel can stop cleanly instead of hanging the GPU.
 #pragma once
 
 #include <cstdint>
@@ -86,12 +86,6 @@ enum StatusBits : uint32_t {
   kStatusWaitTimeout = 4u,   // an mbarrier wait ran out of time; the kernel stopped early
 };
 
-__device__ __forceinline__ uint64_t global_timer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // ----------------------------------------------------------------- shared-memory addresses
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -142,18 +136,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait for the phase with the given parity to complete, for at most `limit_ns`.
-// On timeout: set kStatusWaitTimeout in *status (if non-null) and return false.
+// Wait for the phase with the given parity to complete, for at most `limit_cycles` SM
+// clock cycles (about a second at B200 clocks). The bound is kept with the SM's own cycle
+// counter, which is cheap to read, and only checked every 256 polls. On timeout: set
+// kStatusWaitTimeout in *status (if non-null) and return false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint32_t* status,
-                                                  uint64_t limit_ns) {
+                                                  uint64_t limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_timer_ns();
+  const uint64_t start = clock64();
   for (;;) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < 256; ++i) {
       if (mbar_try_wait(bar, parity)) return true;
     }
-    if (global_timer_ns() - start > limit_ns) {
+    if (static_cast<uint64_t>(clock64()) - start > limit_cycles) {
       if (status) atomicOr(status, kStatusWaitTimeout);
       return false;
     }
@@ -181,6 +177,27 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// 3-D tiled TMA load of one box into shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint32_t bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// ----------------------------------------------------------------- shared-memory vectors
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 // ----------------------------------------------------------------- ldmatrix / movmatrix / mma

@@ -62,7 +62,7 @@ constexpr int kGenThreads = 128;
 constexpr int kGenChunk = 32;     // tokens per step of the generic kernel
 constexpr int kMaxBatch = 16384;  // the plan lives in shared memory
 constexpr int kMaxHeadGroups = 4; // query-head groups per KV head (counter stride)
-constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr uint64_t kWaitLimit = 2000000000ull;  // SM cycles: about one second at 1.9 GHz
 
 struct DecodeArgs {
   void* out;
@@ -305,10 +305,9 @@ template <typename T, int D, int NT>
 __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                                   const __grid_constant__ CUtensorMap tmv,
                                                                   const DecodeArgs a, const TcShape cfg) {
-  constexpr int KS = D / 16;   // k-steps of K.Q^T, m-tiles of V^T.P^T
-  constexpr int NCH = D / 64;  // 128-byte chunks of one token row of one head
+  constexpr int NCH = D / 64;  // 128-byte pieces of one head's row of K (or V)
+  constexpr int KS = D / 16;   // k-steps of K.Q^T, and m-tiles of V^T.P^T
   constexpr int HPW = 8 * NT;  // query heads per consumer warp
-  constexpr uint32_t kChunkBytes = kTile * 128;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -322,13 +321,16 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   int* misc = reinterpret_cast<int*>(smem + L.misc);
   int* prefix = reinterpret_cast<int*>(smem + L.prefix);
   int* lens = reinterpret_cast<int*>(smem + L.lens);
+  // A stage half holds the tile as rows of 128 bytes, row r = (token * HT + head) * NCH + piece,
+  // in the TMA's 128-byte swizzle: 16-byte unit u of row r sits at unit u ^ (r & 7).
+  const int rows_per_tok = HT * NCH;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < nstage; ++s) {
-      mbar_init(bars + 8u * s, 1);                    // full: the producer's expect_tx arrival
-      mbar_init(bars + 8u * (nstage + s), HT * HG);   // empty: every warp that reads the stage
+      mbar_init(bars + 8u * s, 1);                   // full: the producer's expect_tx arrival
+      mbar_init(bars + 8u * (nstage + s), HT * HG);  // empty: every warp that reads the stage
     }
     fence_barrier_init();
   }
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   volatile int* abort_flag = misc + 2;
 
   if (warp == kCW) {
-    // ---------------- producer warp: one tile (all HT heads, K and V) per stage
+    // ---------------- producer warp: one 3-D TMA box per tensor per tile (per page for page size 8)
     Walk w;
     walk_init(a, misc, w);
     Seg s;
@@ -348,8 +350,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     const uint64_t policy = l2_policy_evict_first();
     const int p_rows = cfg.p_rows;
     const int nsub = kTile / p_rows;
-    const int n_tma = 2 * HT * NCH * nsub;
-    const uint32_t sub_bytes = 2u * HT * NCH * p_rows * 128u;
+    const uint32_t sub_bytes = 2u * p_rows * rows_per_tok * 128u;
     bool ok = true;
     while (ok && walk_next(a, lens, prefix, w, s)) {
       const int ntok = s.tok_end - s.tok_begin;
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       const int ntiles = (ntok + kTile - 1) / kTile;
       const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.b) * a.bt_stride;
       const int last_page = (s.tok_end - 1) / a.page_size;
-      const int x0 = s.u * HT * D;
+      const int piece0 = s.u * rows_per_tok;
       // 32 consecutive block-table entries cached one per lane, the next 32 prefetched.
       int cur_base = INT_MIN / 2, nxt_base = INT_MIN / 2;
       int32_t cur = 0, nxt = 0;
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         const int stage = static_cast<int>(gt % nstage);
         const uint32_t full = bars + 8u * stage;
         const uint32_t empty = bars + 8u * (nstage + stage);
-        if (*abort_flag || !mbar_wait_bounded(empty, ((gt / nstage) & 1u) ^ 1u, a.sync, kWaitLimitNs)) {
+        if (*abort_flag || !mbar_wait_bounded(empty, ((gt / nstage) & 1u) ^ 1u, a.sync, kWaitLimit)) {
           *abort_flag = 1;
           ok = false;
           break;
@@ -401,20 +402,18 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
             y1 = y;
           }
         }
-        if (lane == 0) mbar_arrive_expect_tx(full, (v0 ? sub_bytes : 0u) + (v1 ? sub_bytes : 0u));
-        __syncwarp();
-        const uint32_t sbase = ring + stage * L.stage_bytes;
-        for (int idx = lane; idx < n_tma; idx += 32) {
-          const int r = idx % nsub;
-          int rest = idx / nsub;
-          const int c = rest % NCH;
-          rest /= NCH;
-          const int ht = rest % HT;
-          const int tensor = rest / HT;
-          if (!(r ? v1 : v0)) continue;
-          const uint32_t dst = sbase + tensor * L.half + ht * L.head_bytes + c * kChunkBytes + r * p_rows * 128u;
-          tma_load_2d(dst, tensor ? static_cast<const void*>(&tmv) : static_cast<const void*>(&tmk),
-                      x0 + ht * D + c * 64, r ? y1 : y0, full, policy);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full, (v0 ? sub_bytes : 0u) + (v1 ? sub_bytes : 0u));
+          const uint32_t sbase = ring + stage * L.stage_bytes;
+          if (v0) {
+            tma_load_3d(sbase, &tmk, 0, piece0, y0, full, policy);
+            tma_load_3d(sbase + L.half, &tmv, 0, piece0, y0, full, policy);
+          }
+          if (v1) {
+            const uint32_t off = p_rows * rows_per_tok * 128u;
+            tma_load_3d(sbase + off, &tmk, 0, piece0, y1, full, policy);
+            tma_load_3d(sbase + L.half + off, &tmv, 0, piece0, y1, full, policy);
+          }
         }
         __syncwarp();
       }
@@ -422,24 +421,26 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     // Let every copy this CTA issued land before the CTA may exit.
     const uint32_t inflight = min(gt, static_cast<uint32_t>(nstage));
     for (uint32_t k = gt - inflight; k < gt; ++k) {
-      mbar_wait_bounded(bars + 8u * (k % nstage), (k / nstage) & 1u, a.sync, kWaitLimitNs);
+      mbar_wait_bounded(bars + 8u * (k % nstage), (k / nstage) & 1u, a.sync, kWaitLimit);
     }
     return;
   }
 
   // ---------------- consumer warps (threads 0..255)
+  //
+  // Fragments come from plain 16-byte shared loads. The contraction index of S = K.Q^T is
+  // permuted (identically for K and Q): k-step j = 2*kk + jj covers, for lane (g, t4),
+  // d = 32*kk + 8*t4 + 4*jj + {0,1} (cols 2t4, 2t4+1) and + {2,3} (cols 2t4+8, 2t4+9), so a
+  // lane's 16 contiguous bytes of a K row feed two k-steps. The output-row index of
+  // O^T = V^T.P^T is permuted too: m-tile 4*c + mt, row g holds d = 64*c + 8*g + 2*mt and
+  // row g+8 holds d + 1, so a lane reads one 16-byte unit of V per token and ends up owning
+  // 8 consecutive output values per head.
   zero_empty_sequences<T>(a, lens, threadIdx.x, kCW * 32);
   const int ht = warp % HT;
   const int hg = (warp / HT) % HG;
   const int tw = warp / (HT * HG);
   const int mu = ht * HG + hg;  // (head, group) within the unit: slot and barrier index
   const int g = lane >> 2, t4 = lane & 3;
-  const int mi = lane >> 3, r8 = lane & 7;
-  // ldmatrix row addresses: K (A operand of S = K.Q^T) and V (A operand of O^T = V^T.P^T, transposed).
-  const uint32_t k_row = (r8 + 8 * (mi & 1)) * 128u;
-  const int k_half = mi >> 1;
-  const uint32_t v_row = (r8 + 8 * (mi >> 1)) * 128u;
-  const int v_half = mi & 1;
   const float sl = a.scale_log2;
   const int G = a.group;
 
@@ -452,18 +453,21 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     const int ntiles = (ntok + kTile - 1) / kTile;
     const int kvh = s.u * HT + ht;
 
-    // Q^T as the B operand: lane holds q[head g][2t4, 2t4+1] and [2t4+8, 2t4+9] of each k-step.
+    // Q^T as the B operand, in the permuted contraction order: one 16-byte load per 32 d.
     uint32_t qf[KS][NT][2];
     const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int h = hg * HPW + nt * 8 + g;
       const bool hv = h < G;
-      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qb + static_cast<int64_t>(hv ? h : 0) * D);
+      const uint4* qrow = reinterpret_cast<const uint4*>(qb + static_cast<int64_t>(hv ? h : 0) * D);
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        qf[ks][nt][0] = hv ? __ldg(qrow + ks * 8 + t4) : 0u;
-        qf[ks][nt][1] = hv ? __ldg(qrow + ks * 8 + 4 + t4) : 0u;
+      for (int kk = 0; kk < D / 32; ++kk) {
+        const uint4 v = hv ? __ldg(qrow + kk * 4 + t4) : make_uint4(0u, 0u, 0u, 0u);
+        qf[2 * kk][nt][0] = v.x;
+        qf[2 * kk][nt][1] = v.y;
+        qf[2 * kk + 1][nt][0] = v.z;
+        qf[2 * kk + 1][nt][1] = v.w;
       }
     }
 
@@ -480,12 +484,12 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       const uint32_t gj = gt + j;
       const int stage = static_cast<int>(gj % nstage);
       if (*abort_flag) break;
-      if (!mbar_wait_bounded(bars + 8u * stage, (gj / nstage) & 1u, a.sync, kWaitLimitNs)) {
+      if (!mbar_wait_bounded(bars + 8u * stage, (gj / nstage) & 1u, a.sync, kWaitLimit)) {
         *abort_flag = 1;
         break;
       }
       const int valid = min(kTile, ntok - j * kTile);
-      const uint32_t sk = ring + stage * L.stage_bytes + ht * L.head_bytes;
+      const uint32_t sk = ring + stage * L.stage_bytes;
       const uint32_t sv = sk + L.half;
 
       // S = K . Q^T : [16 tokens x 8 heads] per n-tile.
@@ -493,11 +497,21 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
 #pragma unroll
-      for (int ks = 0; ks < KS; ++ks) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(sk + (ks >> 2) * kChunkBytes + k_row + (((((2 * ks) & 7) + k_half) ^ r8) << 4), a0, a1, a2, a3);
+      for (int c = 0; c < NCH; ++c) {
+        const int ra = (g * HT + ht) * NCH + c;        // token g
+        const int rb = ((g + 8) * HT + ht) * NCH + c;  // token g + 8
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(sc[nt], a0, a1, a2, a3, qf[ks][nt][0], qf[ks][nt][1]);
+        for (int par = 0; par < 2; ++par) {
+          const int u = par * 4 + t4;
+          const uint4 x = lds128(sk + ra * 128 + ((u ^ (ra & 7)) << 4));
+          const uint4 y = lds128(sk + rb * 128 + ((u ^ (rb & 7)) << 4));
+          const int j0 = 4 * c + 2 * par;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            Mma<T>::run(sc[nt], x.x, y.x, x.y, y.y, qf[j0][nt][0], qf[j0][nt][1]);
+            Mma<T>::run(sc[nt], x.z, y.z, x.w, y.w, qf[j0 + 1][nt][0], qf[j0 + 1][nt][1]);
+          }
+        }
       }
 
       // Online softmax in base 2. Lane holds tokens g and g+8 of heads 2*t4 and 2*t4+1.
@@ -540,23 +554,30 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         pb[nt][1] = movmatrix_trans(p23);
       }
 
-      // O^T += V^T . P^T ; rows of V past the valid tokens are zeroed, never multiplied.
-      uint32_t m01 = 0xffffffffu, m23 = 0xffffffffu;
-      if (valid < kTile) {
-        m01 = (2 * t4 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 1 < valid ? 0xffff0000u : 0u);
-        m23 = (2 * t4 + 8 < valid ? 0x0000ffffu : 0u) | (2 * t4 + 9 < valid ? 0xffff0000u : 0u);
-      }
+      // O^T += V^T . P^T ; V rows past the valid tokens are zeroed, never multiplied.
 #pragma unroll
-      for (int mt = 0; mt < KS; ++mt) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(sv + (mt >> 2) * kChunkBytes + v_row + (((((2 * mt) & 7) + v_half) ^ r8) << 4), a0, a1, a2,
-                      a3);
-        a0 &= m01;
-        a1 &= m01;
-        a2 &= m23;
-        a3 &= m23;
+      for (int c = 0; c < NCH; ++c) {
+        uint4 v[4];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(acc[mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int tok = 2 * t4 + (q4 & 1) + 8 * (q4 >> 1);  // 2t4, 2t4+1, 2t4+8, 2t4+9
+          const int r = (tok * HT + ht) * NCH + c;
+          v[q4] = lds128(sv + r * 128 + ((g ^ (r & 7)) << 4));
+          if (tok >= valid) v[q4] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        const uint32_t va[4] = {v[0].x, v[0].y, v[0].z, v[0].w};
+        const uint32_t vb[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
+        const uint32_t vc[4] = {v[2].x, v[2].y, v[2].z, v[2].w};
+        const uint32_t vd[4] = {v[3].x, v[3].y, v[3].z, v[3].w};
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          const uint32_t a0 = __byte_perm(va[mt], vb[mt], 0x5410);
+          const uint32_t a1 = __byte_perm(va[mt], vb[mt], 0x7632);
+          const uint32_t a2 = __byte_perm(vc[mt], vd[mt], 0x5410);
+          const uint32_t a3 = __byte_perm(vc[mt], vd[mt], 0x7632);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(acc[c * 4 + mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + 8u * (nstage + stage));
@@ -576,6 +597,8 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       }
     }
 
+    // Lane (g, t4) owns, for head hl = nt*8 + 2*t4 + e and piece c, output d = 64c + 8g + k,
+    // k = 0..7, held in acc[4c + k/2][nt][e + 2*(k & 1)].
     // Warps that split the tiles of one (head, group) combine into the tw == 0 warp.
     if (TW > 1) {
       if (tw != 0) {
@@ -592,9 +615,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
               rl[hl] = l_run[nt][e];
             }
 #pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
-              ra[hl * (D + 4) + mt * 16 + g] = acc[mt][nt][e];
-              ra[hl * (D + 4) + mt * 16 + g + 8] = acc[mt][nt][2 + e];
+            for (int c = 0; c < NCH; ++c) {
+              float* dst = ra + hl * (D + 4) + c * 64 + 8 * g;
+#pragma unroll
+              for (int k = 0; k < 8; ++k) dst[k] = acc[c * 4 + (k >> 1)][nt][e + 2 * (k & 1)];
             }
           }
         }
@@ -622,11 +646,11 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
               if (m2 == -INFINITY) continue;
               const float f = fast_exp2(m2 - M);
               l += red_l[w2 * HPW + hl] * f;
-              const float* ra = red_acc + (w2 * HPW + hl) * (D + 4);
+              const float* src = red_acc + (w2 * HPW + hl) * (D + 4);
 #pragma unroll
-              for (int mt = 0; mt < KS; ++mt) {
-                acc[mt][nt][e] += ra[mt * 16 + g] * f;
-                acc[mt][nt][2 + e] += ra[mt * 16 + g + 8] * f;
+              for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) acc[c * 4 + (k >> 1)][nt][e + 2 * (k & 1)] += src[c * 64 + 8 * g + k] * f;
               }
             }
             m_run[nt][e] = M;
@@ -651,9 +675,13 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           const float inv = l_run[nt][e] > 0.0f ? 1.0f / l_run[nt][e] : 0.0f;
           T* orow = out + (out_row0 + hl) * D;
 #pragma unroll
-          for (int mt = 0; mt < KS; ++mt) {
-            orow[mt * 16 + g] = Storage<T>::store(acc[mt][nt][e] * inv);
-            orow[mt * 16 + g + 8] = Storage<T>::store(acc[mt][nt][2 + e] * inv);
+          for (int c = 0; c < NCH; ++c) {
+            uint4 pk;
+            pk.x = Storage<T>::pack2(acc[c * 4 + 0][nt][e] * inv, acc[c * 4 + 0][nt][e + 2] * inv);
+            pk.y = Storage<T>::pack2(acc[c * 4 + 1][nt][e] * inv, acc[c * 4 + 1][nt][e + 2] * inv);
+            pk.z = Storage<T>::pack2(acc[c * 4 + 2][nt][e] * inv, acc[c * 4 + 2][nt][e + 2] * inv);
+            pk.w = Storage<T>::pack2(acc[c * 4 + 3][nt][e] * inv, acc[c * 4 + 3][nt][e + 2] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 64 + 8 * g) = pk;
           }
         }
       }
@@ -669,9 +697,12 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
         float* po = a.part_o + (slot * HPW + hl) * D;
 #pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-          po[mt * 16 + g] = acc[mt][nt][e] * inv;
-          po[mt * 16 + g + 8] = acc[mt][nt][2 + e] * inv;
+        for (int c = 0; c < NCH; ++c) {
+          float4* dst = reinterpret_cast<float4*>(po + c * 64 + 8 * g);
+          dst[0] = make_float4(acc[c * 4 + 0][nt][e] * inv, acc[c * 4 + 0][nt][e + 2] * inv,
+                               acc[c * 4 + 1][nt][e] * inv, acc[c * 4 + 1][nt][e + 2] * inv);
+          dst[1] = make_float4(acc[c * 4 + 2][nt][e] * inv, acc[c * 4 + 2][nt][e + 2] * inv,
+                               acc[c * 4 + 3][nt][e] * inv, acc[c * 4 + 3][nt][e + 2] * inv);
         }
         if (g == 0) a.part_lse[slot * HPW + hl] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
       }
@@ -710,11 +741,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           }
         }
         const float inv = W > 0.0f ? 1.0f / W : 0.0f;
-        T* orow = out + (out_row0 + hl) * D + d4;
-        orow[0] = Storage<T>::store(O.x * inv);
-        orow[1] = Storage<T>::store(O.y * inv);
-        orow[2] = Storage<T>::store(O.z * inv);
-        orow[3] = Storage<T>::store(O.w * inv);
+        uint2 pk;
+        pk.x = Storage<T>::pack2(O.x * inv, O.y * inv);
+        pk.y = Storage<T>::pack2(O.z * inv, O.w * inv);
+        *reinterpret_cast<uint2*>(out + (out_row0 + hl) * D + d4) = pk;
       }
       if (lane == 0) atomicExch(counter, 0u);
     }
@@ -1098,18 +1128,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return g_encode;
 }
 
-// 2-D view of one cache: rows = every token slot of the pool, columns = Hkv*D elements.
-// Box = 64 columns (128 bytes) x p_rows rows, 128-byte swizzle.
-bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_tokens, int Hkv, int D, int p_rows) {
+// 3-D view of one cache: (64 elements = 128 bytes) x (Hkv*D/64 pieces of a token row, 128 B apart)
+// x (every token slot of the pool, Hkv*D*2 bytes apart). A box of HT*D/64 pieces x p_rows
+// tokens is one tile of a head block: for HT == Hkv a whole page, read front to back.
+bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_tokens, int Hkv, int D, int HT,
+                   int p_rows) {
   auto enc = encoder();
   if (!enc) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(Hkv) * D, static_cast<cuuint64_t>(pool_tokens)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(Hkv) * D * 2};
-  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(p_rows)};
-  const cuuint32_t estr[2] = {1u, 1u};
+  const cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(Hkv) * D / 64, static_cast<cuuint64_t>(pool_tokens)};
+  const cuuint64_t strides[2] = {128u, static_cast<cuuint64_t>(Hkv) * D * 2};
+  const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(HT * D / 64), static_cast<cuuint32_t>(p_rows)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUtensorMapDataType dt =
       dtype == KL_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+  const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -1147,16 +1179,16 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   if (bt_stride < 0 || (batch > 1 && bt_stride < max_pages)) return static_cast<int>(cudaErrorInvalidValue);
   Plan p;
   if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p)) return rc;
-  // The tensor-core path needs 16-byte aligned caches (TMA), 4-byte aligned q and
-  // TMA row coordinates that fit in int32; otherwise take the generic kernel.
-  const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 4) &&
+  // The tensor-core path needs 16-byte aligned caches (TMA), q and out (vector loads and
+  // stores) and TMA row coordinates that fit in int32; otherwise take the generic kernel.
+  const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 16) && aligned(out, 16) &&
                      (num_pages < 0 || num_pages * P <= INT_MAX);
   CUtensorMap tmk, tmv;
   bool use_tc = false;
   if (tc_ok) {
     const int64_t pool_tokens = num_pages >= 0 ? std::max<int64_t>(num_pages, 1) * P : (int64_t(1) << 31) - 1;
-    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.p_rows) &&
-             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.p_rows);
+    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows) &&
+             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows);
   }
   if (!use_tc && p.tc) {
     if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, true, p)) return rc;
