@@ -113,6 +113,35 @@ int kl_paged_decode_attention(int dtype, void* out, const void* q, const void* k
  */
 int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* stream);
 
+/* Bytes of device memory the library reserves per GPU for kl_paged_decode_noalloc. */
+#define KL_NOALLOC_SCRATCH_BYTES ((16u << 20) + (256u << 10))
+
+/*
+ * kl_paged_decode for callers that cannot allocate device memory when they call it: a
+ * server whose GPU memory was handed out to its own pools at start-up, a runtime that has
+ * reserved every free byte for the KV cache, or a step loop that must never call
+ * cudaMalloc. It allocates nothing; the caller passes inputs and outputs only. Scratch is
+ * one fixed array in this library's device memory, KL_NOALLOC_SCRATCH_BYTES per GPU
+ * (16 MiB of split partials + 256 KiB of counters), held from library load until process
+ * exit.
+ *
+ * - A problem whose scratch (kl_paged_decode_workspace_size) exceeds that array is rejected
+ *   with cudaErrorMemoryAllocation before anything is launched (batch 64, context 4096,
+ *   32/8 heads of 128 fit with room to spare).
+ * - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *   with that device current; make that first call before capturing any stream.
+ * - Every call on a device shares the one array and leaves its contents behind; each call
+ *   zeroes the counters it needs (a cudaMemsetAsync on `stream`) before its kernel. Calls
+ *   that overlap on the GPU (other streams, other host threads) race on the array: run
+ *   them in one stream order.
+ * Arguments and results are those of kl_paged_decode without the scratch buffers.
+ * No counterpart in kernel-lab.
+ */
+int kl_paged_decode_noalloc(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                            const int32_t* block_table, const int32_t* seq_lens, int batch, int num_q_heads,
+                            int num_kv_heads, int head_dim, int page_size, int64_t block_table_stride,
+                            int max_pages_per_seq, int64_t num_pages, float scale, int num_splits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1319,3 +1319,81 @@ int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* s
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------- no-allocation entry point
+//
+// Decode with scratch that lives in this library's own device memory, for callers that
+// cannot allocate device memory at call time: an inference server whose memory is carved
+// up and owned by its pool at start-up, a runtime that has already reserved every free
+// byte for the KV cache, or code that must not call cudaMalloc (or wait on the caching
+// allocator) from inside its step loop. The scratch is one fixed array per GPU, allocated
+// when the library is loaded and held until the process exits.
+
+namespace klb {
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = size_t(16) << 20;  // split partials
+constexpr size_t kNoAllocSyncBytes = size_t(256) << 10;    // status word + arrival counters
+static_assert(kNoAllocPartialBytes + kNoAllocSyncBytes == KL_NOALLOC_SCRATCH_BYTES, "header and library disagree");
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocPartialBytes + kNoAllocSyncBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up on first use there.
+cudaError_t noalloc_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = p;
+  }
+  *ptr = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace klb
+
+extern "C" int kl_paged_decode_noalloc(int dtype, void* out, const void* q, const void* k_cache,
+                                       const void* v_cache, const int32_t* block_table, const int32_t* seq_lens,
+                                       int batch, int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                       int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
+                                       float scale, int num_splits, void* stream) {
+  if (batch == 0) return 0;
+  // Size the scratch of the kernel kl_paged_decode will pick for these pointers: the
+  // tensor-core plan when it applies and the buffers are aligned for it, else the generic one.
+  klb::Plan plan;
+  if (const int rc = klb::make_plan(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size,
+                                    max_pages_per_seq, num_splits, false, plan)) {
+    return rc;
+  }
+  const bool tc_io = klb::aligned(k_cache, 16) && klb::aligned(v_cache, 16) && klb::aligned(q, 16) &&
+                     klb::aligned(out, 16) && (num_pages < 0 || num_pages * page_size <= INT_MAX);
+  if (plan.tc && !tc_io) {
+    if (const int rc = klb::make_plan(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size,
+                                      max_pages_per_seq, num_splits, true, plan)) {
+      return rc;
+    }
+  }
+  const size_t sync_bytes = plan.sync_bytes;
+  if (plan.part_bytes > klb::kNoAllocPartialBytes || sync_bytes > klb::kNoAllocSyncBytes) {
+    return static_cast<int>(cudaErrorMemoryAllocation);  // does not fit the fixed scratch
+  }
+  void* base = nullptr;
+  if (const cudaError_t e = klb::noalloc_scratch(&base)) return static_cast<int>(e);
+  uint8_t* partials = static_cast<uint8_t*>(base);
+  uint8_t* sync = partials + klb::kNoAllocPartialBytes;
+  auto st = static_cast<cudaStream_t>(stream);
+  // The array keeps whatever the previous call left: start from zeroed counters and status.
+  if (const cudaError_t e = cudaMemsetAsync(sync, 0, sync_bytes, st)) return static_cast<int>(e);
+  return kl_paged_decode(dtype, out, q, k_cache, v_cache, block_table, seq_lens, batch, num_q_heads, num_kv_heads,
+                         head_dim, page_size, block_table_stride, max_pages_per_seq, num_pages, scale, num_splits,
+                         partials, klb::kNoAllocPartialBytes, sync, klb::kNoAllocSyncBytes, stream);
+}

@@ -36,6 +36,7 @@ def test_header_declares_the_abi():
         "kl_paged_decode",
         "kl_paged_decode_attention",
         "kl_paged_decode_read_status",
+        "kl_paged_decode_noalloc",
     ]
 
 
