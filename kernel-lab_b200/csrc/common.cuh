@@ -156,6 +156,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// Relaxed GPU-scope load of a flag another CTA updates. Followed by __threadfence() once the
+// value is seen, it forms an acquire (the fence-based acquire pattern of the PTX memory model).
+// Not ordered against earlier memory operations, so it can be issued well before its use.
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // ----------------------------------------------------------------- TMA
 
 // L2 eviction-priority policy for streamed-once data.

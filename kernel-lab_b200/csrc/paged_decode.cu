@@ -453,6 +453,12 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     const int ntiles = (ntok + kTile - 1) / kTile;
     const int kvh = s.u * HT + ht;
 
+    // A split chunk reads how many of its sibling chunks have published already; the load's
+    // latency hides behind this segment's tiles. If all of them have, this chunk is the last
+    // one and merges straight from its registers at the end of the segment.
+    uint32_t published = 0;
+    if (!s.whole && tw == 0 && lane == 0) published = ld_relaxed_gpu(counter_of(a, s.b, kvh, hg));
+
     // Q^T as the B operand, in the permuted contraction order: one 16-byte load per 32 d.
     uint32_t qf[KS][NT][2];
     const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
@@ -687,67 +693,146 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       }
       continue;
     }
-    const int64_t slot = static_cast<int64_t>(s.chunk) * (HT * HG) + mu;
+    // This chunk's normalised partial and base-2 LSE, held in the fragment layout; padding
+    // heads of the last query-head group are never written nor read.
+    float lse_own[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float l = l_run[nt][e];
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        lse_own[nt][e] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+          acc[mt][nt][e] *= inv;
+          acc[mt][nt][e + 2] *= inv;
+        }
+      }
+    }
+    uint32_t* counter = counter_of(a, s.b, kvh, hg);
+    const uint32_t siblings = static_cast<uint32_t>(s.nchunks - 1);
+    bool last = __shfl_sync(0xffffffffu, published, 0) == siblings;
+    if (!last) {
+      const int64_t slot = static_cast<int64_t>(s.chunk) * (HT * HG) + mu;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int hl = nt * 8 + 2 * t4 + e;
+          if (hg * HPW + hl >= G) continue;
+          float* po = a.part_o + (slot * HPW + hl) * D;
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+            float4* dst = reinterpret_cast<float4*>(po + c * 64 + 8 * g);
+            dst[0] = make_float4(acc[c * 4 + 0][nt][e], acc[c * 4 + 0][nt][e + 2], acc[c * 4 + 1][nt][e],
+                                 acc[c * 4 + 1][nt][e + 2]);
+            dst[1] = make_float4(acc[c * 4 + 2][nt][e], acc[c * 4 + 2][nt][e + 2], acc[c * 4 + 3][nt][e],
+                                 acc[c * 4 + 3][nt][e + 2]);
+          }
+          if (g == 0) a.part_lse[slot * HPW + hl] = lse_own[nt][e];
+        }
+      }
+      // Publish: the warp's stores are ordered before lane 0's fence by the warp barrier, and
+      // the fence orders them before the count.
+      __syncwarp();
+      uint32_t before = 0;
+      if (lane == 0) {
+        __threadfence();
+        before = atomicAdd(counter, 1u);
+      }
+      last = __shfl_sync(0xffffffffu, before, 0) == siblings;
+      if (!last) continue;
+    }
+    // Last chunk: acquire the siblings' partials (fence after the observed count), then merge
+    // all chunks in chunk order with a running max, this chunk's own term taken from its
+    // registers (the values it would have stored), so the result does not depend on which
+    // chunk arrived last. A sibling's loads are all issued before any of its arithmetic.
+    if (lane == 0) __threadfence();
+    __syncwarp();
+    float m_acc[NT][2], w_acc[NT][2], o_acc[KS][NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_acc[nt][0] = m_acc[nt][1] = -INFINITY;
+      w_acc[nt][0] = w_acc[nt][1] = 0.0f;
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) o_acc[mt][nt][0] = o_acc[mt][nt][1] = o_acc[mt][nt][2] = o_acc[mt][nt][3] = 0.0f;
+    }
+    for (int k = 0; k < s.nchunks; ++k) {
+      const int ck = chunk_id(a, s, k);
+      const bool own = ck == s.chunk;
+      const int64_t slot2 = static_cast<int64_t>(ck) * (HT * HG) + mu;
+      // Heads whose loads are in flight together: both of a lane's heads when registers allow.
+      constexpr int EG = NT * NCH <= 2 ? 2 : 1;
+#pragma unroll
+      for (int ne = 0; ne < NT * 2; ne += EG) {
+        const int nt = ne / 2;
+        float lse[EG];
+        float4 x[EG][NCH][2];
+#pragma unroll
+        for (int ei = 0; ei < EG; ++ei) {
+          const int e = ne % 2 + ei;
+          const int hl = nt * 8 + 2 * t4 + e;
+          const bool ld = !own && hg * HPW + hl < G;
+          const float* po = a.part_o + (slot2 * HPW + hl) * D;
+          lse[ei] = own ? lse_own[nt][e] : ld ? __ldcg(a.part_lse + slot2 * HPW + hl) : -INFINITY;
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float* lo = &acc[c * 4 + 2 * h][nt][0];
+              const float* hi = &acc[c * 4 + 2 * h + 1][nt][0];
+              x[ei][c][h] = own ? make_float4(lo[e], lo[e + 2], hi[e], hi[e + 2])
+                          : ld  ? __ldcg(reinterpret_cast<const float4*>(po + c * 64 + 8 * g + 4 * h))
+                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+          }
+        }
+#pragma unroll
+        for (int ei = 0; ei < EG; ++ei) {
+          const int e = ne % 2 + ei;
+          const float mn = fmaxf(m_acc[nt][e], lse[ei]);
+          if (mn == -INFINITY) continue;
+          const float fa = fast_exp2(m_acc[nt][e] - mn), fb = fast_exp2(lse[ei] - mn);
+          m_acc[nt][e] = mn;
+          w_acc[nt][e] = w_acc[nt][e] * fa + fb;
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float* lo = &o_acc[c * 4 + 2 * h][nt][0];
+              float* hi = &o_acc[c * 4 + 2 * h + 1][nt][0];
+              lo[e] = lo[e] * fa + fb * x[ei][c][h].x;
+              lo[e + 2] = lo[e + 2] * fa + fb * x[ei][c][h].y;
+              hi[e] = hi[e] * fa + fb * x[ei][c][h].z;
+              hi[e + 2] = hi[e + 2] * fa + fb * x[ei][c][h].w;
+            }
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int hl = nt * 8 + 2 * t4 + e;
-        const float l = l_run[nt][e];
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        float* po = a.part_o + (slot * HPW + hl) * D;
+        if (hg * HPW + hl >= G) continue;
+        const float inv = w_acc[nt][e] > 0.0f ? 1.0f / w_acc[nt][e] : 0.0f;
+        T* orow = out + (out_row0 + hl) * D;
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
-          float4* dst = reinterpret_cast<float4*>(po + c * 64 + 8 * g);
-          dst[0] = make_float4(acc[c * 4 + 0][nt][e] * inv, acc[c * 4 + 0][nt][e + 2] * inv,
-                               acc[c * 4 + 1][nt][e] * inv, acc[c * 4 + 1][nt][e + 2] * inv);
-          dst[1] = make_float4(acc[c * 4 + 2][nt][e] * inv, acc[c * 4 + 2][nt][e + 2] * inv,
-                               acc[c * 4 + 3][nt][e] * inv, acc[c * 4 + 3][nt][e + 2] * inv);
+          uint4 pk;
+          pk.x = Storage<T>::pack2(o_acc[c * 4 + 0][nt][e] * inv, o_acc[c * 4 + 0][nt][e + 2] * inv);
+          pk.y = Storage<T>::pack2(o_acc[c * 4 + 1][nt][e] * inv, o_acc[c * 4 + 1][nt][e + 2] * inv);
+          pk.z = Storage<T>::pack2(o_acc[c * 4 + 2][nt][e] * inv, o_acc[c * 4 + 2][nt][e + 2] * inv);
+          pk.w = Storage<T>::pack2(o_acc[c * 4 + 3][nt][e] * inv, o_acc[c * 4 + 3][nt][e + 2] * inv);
+          *reinterpret_cast<uint4*>(orow + c * 64 + 8 * g) = pk;
         }
-        if (g == 0) a.part_lse[slot * HPW + hl] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
       }
     }
-    __threadfence();
-    __syncwarp();
-    uint32_t* counter = counter_of(a, s.b, kvh, hg);
-    int last = 0;
-    if (lane == 0) last = atomicAdd(counter, 1u) == static_cast<uint32_t>(s.nchunks - 1);
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      __threadfence();
-      const int nh = min(HPW, G - hg * HPW);
-      for (int i = lane; i < nh * (D / 4); i += 32) {
-        const int hl = i / (D / 4);
-        const int d4 = (i - hl * (D / 4)) * 4;
-        float M = -INFINITY;
-        for (int k = 0; k < s.nchunks; ++k) {
-          const int64_t sk2 = static_cast<int64_t>(chunk_id(a, s, k)) * (HT * HG) + mu;
-          M = fmaxf(M, __ldcg(a.part_lse + sk2 * HPW + hl));
-        }
-        float W = 0.0f;
-        float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (M > -INFINITY) {
-          for (int k = 0; k < s.nchunks; ++k) {
-            const int64_t sk2 = static_cast<int64_t>(chunk_id(a, s, k)) * (HT * HG) + mu;
-            const float lse = __ldcg(a.part_lse + sk2 * HPW + hl);
-            if (lse == -INFINITY) continue;
-            const float f = fast_exp2(lse - M);
-            const float4 o = __ldcg(reinterpret_cast<const float4*>(a.part_o + (sk2 * HPW + hl) * D + d4));
-            W += f;
-            O.x += f * o.x;
-            O.y += f * o.y;
-            O.z += f * o.z;
-            O.w += f * o.w;
-          }
-        }
-        const float inv = W > 0.0f ? 1.0f / W : 0.0f;
-        uint2 pk;
-        pk.x = Storage<T>::pack2(O.x * inv, O.y * inv);
-        pk.y = Storage<T>::pack2(O.z * inv, O.w * inv);
-        *reinterpret_cast<uint2*>(out + (out_row0 + hl) * D + d4) = pk;
-      }
-      if (lane == 0) atomicExch(counter, 0u);
-    }
+    // Every sibling has counted (or none needed to): nobody else touches the counter in this
+    // launch, so a plain store returns it to zero for the next one.
+    if (lane == 0) *reinterpret_cast<volatile uint32_t*>(counter) = 0u;
   }
 }
 
