@@ -319,25 +319,35 @@ def main() -> None:
     if world > 1:
         dist.barrier()
 
-    # ---- timed region: exactly K steps, CUDA events on the launching stream
-    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # ---- timed region: exactly K steps, CUDA events on the launching stream. On one GPU a
+    # step is exactly one launch of the kernel, so the region's two events give the kernel's
+    # average launch duration (an event between back-to-back launches would add ~5 us of
+    # launch gap to every step); with a gather in the step, events bracket each kernel too.
+    per_kernel = world > 1 and spec["kind"] == "decode"
+    n_ev = args.steps if per_kernel else 0
+    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
         torch.cuda.synchronize()
         t0.record(stream)
         for i in range(args.steps):
-            k_start[i].record(stream)
-            kernel()
-            k_end[i].record(stream)
-            if world > 1 and spec["kind"] == "decode":
+            if per_kernel:
+                k_start[i].record(stream)
+                kernel()
+                k_end[i].record(stream)
                 gather_heads(out_local, world, out=out_full)
+            else:
+                step()
         t1.record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     step_ms = t0.elapsed_time(t1) / args.steps
-    kern_ms = sum(a.elapsed_time(b) for a, b in zip(k_start, k_end, strict=True)) / args.steps
+    if per_kernel:
+        kern_ms = sum(a.elapsed_time(b) for a, b in zip(k_start, k_end, strict=True)) / args.steps
+    else:
+        kern_ms = step_ms
     tt = torch.tensor([step_ms, kern_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -346,23 +356,56 @@ def main() -> None:
     # ---- end to end through the torch op: pinned host inputs in, result out, every step
     e2e = None
     if spec["kind"] == "decode":
+        # A serving loop's shape: two device slots; step i's inputs go up on a copy-in stream
+        # and its output comes back on a copy-out stream, so copies overlap the neighbouring
+        # steps' kernels. Every step still copies its own q, block table and lengths in and
+        # its whole output out; the KV cache stays resident.
         q_h = q.cpu().pin_memory()
         bt_h = kv.block_table.cpu().pin_memory()
         ln_h = kv.seq_lens.cpu().pin_memory()
-        out_h = torch.empty(out_full.shape if world > 1 else out_local.shape, dtype=q.dtype).pin_memory()
+        out_shape = out_full.shape if world > 1 else out_local.shape
+        out_hs = [torch.empty(out_shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+        slots = [dict(q=torch.empty_like(q), bt=torch.empty_like(kv.block_table), ln=torch.empty_like(kv.seq_lens),
+                      out=torch.empty_like(out_local),
+                      full=torch.empty(out_shape, dtype=q.dtype, device=dev) if world > 1 else None,
+                      inputs_free=None, out_read=None) for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
         h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + ln_h.numel() * 4
-        d2h = out_h.numel() * out_h.element_size()
+        d2h = out_hs[0].numel() * out_hs[0].element_size()
+        e2e_count = [0]
 
         def e2e_step():
-            q.copy_(q_h, non_blocking=True)
-            kv.block_table.copy_(bt_h, non_blocking=True)
-            kv.seq_lens.copy_(ln_h, non_blocking=True)
-            torch.ops.kernel_lab.paged_decode_attention(out_local, q, kv.k_cache, kv.v_cache, kv.block_table,
-                                                        kv.seq_lens, scale)
-            src = out_local
-            if world > 1:
-                src = gather_heads(out_local, world, out=out_full)
-            out_h.copy_(src, non_blocking=True)
+            i = e2e_count[0]
+            e2e_count[0] += 1
+            sl = slots[i % 2]
+            with torch.cuda.stream(s_in):
+                if sl["inputs_free"] is not None:
+                    s_in.wait_event(sl["inputs_free"])  # the kernel two steps back is done with them
+                sl["q"].copy_(q_h, non_blocking=True)
+                sl["bt"].copy_(bt_h, non_blocking=True)
+                sl["ln"].copy_(ln_h, non_blocking=True)
+                arrived = torch.cuda.Event()
+                arrived.record(s_in)
+            stream.wait_event(arrived)
+            if sl["out_read"] is not None:
+                stream.wait_event(sl["out_read"])  # the copy-out two steps back has read the slot
+            torch.ops.kernel_lab.paged_decode_attention(sl["out"], sl["q"], kv.k_cache, kv.v_cache, sl["bt"],
+                                                        sl["ln"], scale)
+            src = sl["out"] if world == 1 else gather_heads(sl["out"], world, out=sl["full"])
+            done = torch.cuda.Event()
+            done.record(stream)
+            sl["inputs_free"] = done
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                out_hs[i % 2].copy_(src, non_blocking=True)
+                read = torch.cuda.Event()
+                read.record(s_out)
+            sl["out_read"] = read
+
+        def e2e_join():
+            for sl in slots:
+                if sl["out_read"] is not None:
+                    stream.wait_event(sl["out_read"])
     else:
         x_h = x.cpu().pin_memory()
         res_h = res.cpu().pin_memory()
@@ -378,6 +421,9 @@ def main() -> None:
             out_h.copy_(out, non_blocking=True)
             res_back.copy_(res, non_blocking=True)
 
+        def e2e_join():
+            pass
+
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize()
@@ -386,14 +432,23 @@ def main() -> None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_steps = max(10, min(args.steps, 100))
     e0.record(stream)
+    if spec["kind"] == "decode":
+        s_in.wait_event(e0)  # no copy of the timed steps starts before the region does
     for _ in range(e2e_steps):
         e2e_step()
+    e2e_join()
     e1.record(stream)
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = te.item()
+    if spec["kind"] == "decode":
+        # The pipelined steps computed what the resident steps did (same inputs, deterministic
+        # kernel): a copy that raced its slot would show here.
+        ref = (out_full if world > 1 else out_local).cpu()
+        if not torch.equal(out_hs[(e2e_count[0] - 1) % 2], ref):
+            raise SystemExit("e2e output differs from the device-resident step's output")
     e2e = {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d * world),
            "d2h_bytes_per_step": int(d2h * (1 if spec["kind"] == "decode" else world)), "ms_per_step": e2e_ms}
 

@@ -8,32 +8,37 @@
 //
 // Work decomposition. A "tile" is 16 tokens of one sequence for one "unit" of heads: a
 // block of HT consecutive KV heads in the tensor-core kernel, one KV head in the generic
-// one. Every CTA computes the same plan from seq_lens (no host sync): the tiles of all
-// (sequence, unit) pairs are laid end to end and CTA c takes the contiguous range
-// [c*R, (c+1)*R), R = max(min_tiles, ceil(total / grid)), so every CTA streams the same
-// number of KV bytes whatever the length distribution (ragged batches included). A
-// (sequence, unit) that a range boundary cuts is split into "chunks": each chunk writes
-// a normalised fp32 partial and its LSE to scratch and bumps an arrival counter; the
-// last chunk to arrive merges them all (nobody waits on another CTA) and resets the
-// counter to zero. A forced split count (num_splits > 0) instead gives every sequence
-// exactly ceil(max_pages / pages_per_split) chunks, including empty ones, like the
-// Triton kernel.
+// one. Every CTA computes the same plan from seq_lens (no host sync): the (sequence, unit)
+// items are laid end to end, each costing its tiles plus a fixed per-item charge (the time
+// a CTA spends starting an item), and CTA c takes the cost range [c*R, (c+1)*R),
+// R = max(min_tiles, ceil(total / grid)), so every CTA streams about the same number of KV
+// bytes whatever the length distribution (ragged batches included). An item that a range
+// boundary cuts is split into "chunks". A chunk reads its item's arrival counter when it
+// starts; if every sibling has already published, it merges their partials with its own
+// registers at the end; otherwise it writes a normalised fp32 partial and base-2 LSE,
+// bumps the counter, and the chunk that completes the count merges. The merge always
+// runs in chunk order, so the result does not depend on arrival order, and it resets the
+// counter to zero; nobody waits on another CTA. A forced split count (num_splits > 0)
+// instead gives every sequence exactly ceil(max_pages / pages_per_split) chunks,
+// including empty ones, like the Triton kernel.
 //
 // Tensor-core kernel (fp16/bf16, head_dim 64/128/256, page size 8 or a multiple of 16).
 // A stage holds the K and V rows of one tile for HT KV heads: with Llama-3-8B's 8 KV
 // heads that is one whole 16-token page, 32 KB of K and 32 KB of V read contiguously,
 // instead of 256-byte per-head rows scattered over the page. One producer warp walks the
-// plan and its 32 lanes issue the stage's 2-D TMA boxes (64 columns x 16 rows, 128-byte
-// swizzle, L2 evict-first) into a ring of shared-memory stages guarded by mbarriers.
-// Eight consumer warps: warp (ht, hg, tw) owns KV head ht of the stage and query-head
-// group hg (8*NT query heads of that KV head's GQA group); when a unit has fewer heads
-// than warps, TW warps split the tiles and combine through shared memory. A consumer
-// computes S = K.Q^T with mma.m16n8k16 (M = 16 tokens, N = 8 query heads, K = head_dim),
-// the online softmax in base 2 on the fp32 fragments, turns P into the B operand with
-// movmatrix, and accumulates O^T += V^T.P^T (V^T via ldmatrix.trans).
+// plan and issues one 3-D TMA box per tensor per tile (128-byte swizzle, L2 evict-first)
+// into a ring of shared-memory stages guarded by mbarriers. Eight consumer warps: warp
+// (ht, hg, tw) owns KV head ht of the stage and query-head group hg (8*NT query heads of
+// that KV head's GQA group); when a unit has fewer heads than warps, TW warps split the
+// tiles and combine through shared memory. A consumer computes S = K.Q^T with
+// mma.m16n8k16 (M = 16 tokens, N = 8 query heads, K = head_dim), the online softmax in
+// base 2 on the fp32 fragments, turns P into the B operand with movmatrix, and
+// accumulates O^T += V^T.P^T. K and V fragments come from plain 16-byte shared loads in a
+// permuted contraction / output-row order, so no ldmatrix is needed.
 //
-// Generic kernel (fp32, other head_dims / page sizes / groups): same plan and merge, CUDA
-// cores, 32-token chunks staged through shared memory.
+// Generic kernel (fp32, other head_dims / page sizes / groups): same plan, CUDA cores,
+// 32-token chunks staged through shared memory; every chunk publishes its partial and the
+// one that completes the count merges them all from scratch, in chunk order.
 //
 // Safety: pages outside [0, num_pages) are skipped and flagged; every mbarrier wait is
 // bounded in time and flags a timeout; the producer lets all its copies land before exit.
@@ -80,6 +85,7 @@ struct DecodeArgs {
   int splits;           // 0: balanced plan; > 0: forced splits per sequence
   int pages_per_split;  // forced mode
   int min_tiles;        // balanced mode: minimum tiles per CTA
+  int seg_cost;         // balanced mode: tiles' worth of time charged for starting a (sequence, unit)
   uint32_t* sync;       // [0] status, [1 + (b*Hkv + kvh)*kMaxHeadGroups + hg] arrival counters
   float* part_o;        // [slot][slot_heads][head_dim]
   float* part_lse;      // [slot][slot_heads]
@@ -113,6 +119,7 @@ struct Seg {
 
 struct Walk {
   int t, t1, R;     // balanced
+  bool first;       // balanced: no segment produced yet
   int item, items;  // forced
 };
 
@@ -126,9 +133,11 @@ __device__ __forceinline__ int clamp_len(const DecodeArgs& a, int b, bool report
   return len < 0 ? 0 : len;
 }
 
-// All threads of the block. lens[b] = clamped length; prefix[b] = tiles of sequences
-// before b; misc[0] = total tiles over all units, misc[1] = R; misc[2] (abort flag) and
-// misc[3] are zeroed; misc[4..35] is scan scratch. Ends with a block barrier.
+// All threads of the block. lens[b] = clamped length; prefix[b] = cost of one unit of every
+// sequence before b, where a non-empty sequence costs its tiles plus seg_cost (the time a
+// CTA spends starting a (sequence, unit): Q loads, partial write and count, merge);
+// misc[0] = total cost over all units, misc[1] = R; misc[2] (abort flag) and misc[3] are
+// zeroed; misc[4..35] is scan scratch. Ends with a block barrier.
 __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* misc) {
   const int B = a.batch;
   const int nt = blockDim.x;
@@ -140,7 +149,7 @@ __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* mis
   for (int i = lo; i < hi; ++i) {
     const int len = clamp_len(a, i, blockIdx.x == 0);
     lens[i] = len;
-    local += (len + kTile - 1) / kTile;
+    local += len > 0 ? (len + kTile - 1) / kTile + a.seg_cost : 0;
   }
   int inc = local;
 #pragma unroll
@@ -166,7 +175,7 @@ __device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* mis
   int run = wtot[warp] + inc - local;
   for (int i = lo; i < hi; ++i) {
     prefix[i] = run;
-    run += (lens[i] + kTile - 1) / kTile;
+    run += lens[i] > 0 ? (lens[i] + kTile - 1) / kTile + a.seg_cost : 0;
   }
   if (tid == 0) {
     const int per_unit = misc[2];
@@ -187,6 +196,7 @@ __device__ __forceinline__ void walk_init(const DecodeArgs& a, const int* misc, 
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * w.R;
     w.t = static_cast<int>(min(t0, static_cast<int64_t>(total)));
     w.t1 = static_cast<int>(min(t0 + w.R, static_cast<int64_t>(total)));
+    w.first = true;
   } else {
     w.item = blockIdx.x;
     w.items = a.batch * a.units * a.splits;
@@ -203,24 +213,31 @@ __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const int* lens, 
       const int mid = (lo + hi + 1) >> 1;
       if (static_cast<int64_t>(U) * prefix[mid] <= w.t) lo = mid; else hi = mid - 1;
     }
+    // b is never empty here: an empty sequence has the same prefix as the next one.
     const int b = lo;
-    const int n = prefix[b + 1] - prefix[b];
+    const int nc = prefix[b + 1] - prefix[b];      // cost of one unit: seg_cost, then the tiles
+    const int n = (lens[b] + kTile - 1) / kTile;  // tiles of one unit
     const int seq0 = U * prefix[b];
-    const int off = w.t - seq0;
-    const int u = off / n, tile = off - u * n;
-    const int len = min(n - tile, w.t1 - w.t);
-    const int s_begin = seq0 + u * n;
-    const int s_end = s_begin + n;
+    const int u = (w.t - seq0) / nc;
+    const int s_begin = seq0 + u * nc;  // the item's cost range [s_begin, s_end) ends with its tiles
+    const int s_end = s_begin + nc;
+    const int ts = s_end - n;
+    if (w.t1 <= ts) return false;  // this range ends before the item's first tile
+    const int from = max(w.t, ts);
+    const int tile = from - ts;
+    const int len = min(s_end, w.t1) - from;
     s.b = b;
     s.u = u;
     s.tok_begin = tile * kTile;
     s.tok_end = min(lens[b], (tile + len) * kTile);
-    s.c_first = s_begin / w.R;
+    s.c_first = ts / w.R;
     s.nchunks = (s_end - 1) / w.R - s.c_first + 1;
-    s.first_aligned = s_begin == s.c_first * w.R;
+    // The first chunk is its CTA's first segment iff that CTA's range holds no earlier tiles.
+    s.first_aligned = s.c_first * w.R >= s_begin;
     s.whole = s.nchunks == 1;
-    s.chunk = w.t == static_cast<int>(blockIdx.x) * w.R ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
-    w.t += len;
+    s.chunk = w.first ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+    w.first = false;
+    w.t = from + len;
     return true;
   }
   if (w.item >= w.items) return false;
@@ -1034,6 +1051,7 @@ struct Plan {
   int units = 0;
   int splits = 0, pps = 0;
   int slots = 0, slot_heads = 0;
+  int seg_cost = 0;
   size_t part_bytes = 0, sync_bytes = 0;
   const void* fn = nullptr;
 };
@@ -1091,9 +1109,14 @@ const void* gen_fn(int dtype) {
 constexpr int kMinTilesPerCta = 4;
 constexpr uint32_t kTcSmemBudget = 200 * 1024;  // one tensor-core CTA per SM
 constexpr int kMaxStages = 24;
+// Balanced plan: tiles' worth of time a tensor-core CTA loses per (sequence, head block) it
+// starts (Q loads, partial write and count). Measured at batch 64 x 4096 tokens: charging 2
+// tiles levels CTAs with one and two segments (158.4 us against 160.4 us with none).
+constexpr int kTcSegmentCost = 2;
 
 // Optional tuning overrides read once from the environment:
-//   KL_DECODE_HEADS_PER_TILE (1/2/4/8), KL_DECODE_STAGES (2..24). 0 = automatic.
+//   KL_DECODE_HEADS_PER_TILE (1/2/4/8), KL_DECODE_STAGES (2..24), KL_DECODE_SEGMENT_COST
+//   (tiles charged per (sequence, unit) start by the balanced plan; negative: none). 0 = automatic.
 int env_int(const char* name) {
   const char* v = std::getenv(name);
   return v ? std::atoi(v) : 0;
@@ -1191,6 +1214,11 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     chunks = 2LL * p.grid;
   }
   if (chunks * slots_per_chunk > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
+  const int forced_cost = env_int("KL_DECODE_SEGMENT_COST");
+  p.seg_cost = forced_cost < 0 ? 0 : forced_cost > 0 ? std::min(forced_cost, 64) : p.tc ? kTcSegmentCost : 0;
+  if (static_cast<int64_t>(batch) * (max_tiles + p.seg_cost) * p.units > INT_MAX / 2) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
   p.slots = static_cast<int>(chunks * slots_per_chunk);
   p.part_bytes = lse_offset(p.slots, p.slot_heads, D) + static_cast<size_t>(p.slots) * p.slot_heads * 4;
   p.sync_bytes = (1 + static_cast<size_t>(batch) * Hkv * kMaxHeadGroups) * 4;
@@ -1302,6 +1330,7 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   a.splits = p.splits;
   a.pages_per_split = p.pps;
   a.min_tiles = kMinTilesPerCta;
+  a.seg_cost = p.seg_cost;
   a.sync = static_cast<uint32_t*>(sync);
   a.part_o = static_cast<float*>(partials);
   a.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + lse_offset(p.slots, p.slot_heads, D));
