@@ -122,6 +122,21 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
       : "memory");
 }
 
+// Non-blocking test: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
@@ -156,14 +171,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
-// Relaxed GPU-scope load of a flag another CTA updates. Followed by __threadfence() once the
-// value is seen, it forms an acquire (the fence-based acquire pattern of the PTX memory model).
+// Relaxed GPU-scope load of a flag another CTA updates. Followed by fence_acq_rel_gpu() once
+// the value is seen, it forms an acquire (the fence-based acquire pattern of the PTX memory model).
 // Not ordered against earlier memory operations, so it can be issued well before its use.
 __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
+
+// GPU-scope release/acquire without a sequentially consistent fence (which costs
+// microseconds when many SMs issue it at once):
+// - atom_add_acq_rel_gpu publishes every write ordered before it (the issuing thread's, and
+//   its warp's through a preceding __syncwarp) and acquires what the previous holders of the
+//   counter published;
+// - fence_acq_rel_gpu after a relaxed load that saw another thread's count acquires that
+//   thread's writes (the fence-based acquire pattern).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 // ----------------------------------------------------------------- TMA
 

@@ -60,7 +60,9 @@
 
 namespace klb {
 
-constexpr int kTile = 16;         // tokens per tile: the MMA's M
+constexpr int kTile = 16;
+constexpr uint32_t kBatchStageBytes = 16 * 1024;  // producer issues tiles in batches up to this stage size
+constexpr int kRegisterMergeChunks = 4;  // splits of at most this many chunks merge from registers         // tokens per tile: the MMA's M
 constexpr int kCW = 8;            // consumer warps of the tensor-core kernel
 constexpr int kTCThreads = 32 * (kCW + 1);
 constexpr int kGenThreads = 128;
@@ -283,6 +285,140 @@ __device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const 
   }
 }
 
+// Merge of a split (sequence, unit, query-head group) by one warp, every chunk's normalised
+// partial and base-2 LSE being in scratch. Lane k reads chunk k's LSEs (32 chunks a round);
+// the per-head max M and weight sum W come from fixed-order warp reductions. Then lane L owns
+// float4 i = L + 32*j (j < NE) of the nh x D outputs and accumulates sum_k 2^(lse_k - M) * o_k
+// in chunk order, with KB chunks' loads in flight at a time and each weight shuffled from its
+// chunk's lane. The result depends only on the partials, never on which chunk merges; it is
+// written as out = sum / W (zero where every chunk was empty). kernel-lab's merge formula
+// (triton_kernels/paged_attention.py:150-166).
+template <typename T, int D, int HPW, int NE, int KB>
+__device__ __forceinline__ void merge_chunks_impl(const DecodeArgs& a, const Seg& s, int slots_per_chunk, int mu,
+                                                  int nh, T* out_rows, int lane) {
+  constexpr int Q = D / 4;  // float4 per head row
+  const int n4 = nh * Q;
+  const int nchunks = s.nchunks;
+  auto part_row = [&](int k) {  // first element (in heads) of chunk k's partial rows for this group
+    return (static_cast<int64_t>(chunk_id(a, s, k)) * slots_per_chunk + mu) * HPW;
+  };
+  auto load_lse = [&](int k, float (&l)[HPW]) {
+#pragma unroll
+    for (int h = 0; h < HPW; ++h) l[h] = -INFINITY;
+    if (k < nchunks) {
+      const float4* p = reinterpret_cast<const float4*>(a.part_lse + part_row(k));
+#pragma unroll
+      for (int h4 = 0; h4 < HPW / 4; ++h4) {
+        const float4 v = __ldcg(p + h4);
+        l[4 * h4 + 0] = 4 * h4 + 0 < nh ? v.x : -INFINITY;
+        l[4 * h4 + 1] = 4 * h4 + 1 < nh ? v.y : -INFINITY;
+        l[4 * h4 + 2] = 4 * h4 + 2 < nh ? v.z : -INFINITY;
+        l[4 * h4 + 3] = 4 * h4 + 3 < nh ? v.w : -INFINITY;
+      }
+    }
+  };
+  float4 x[KB][NE];
+  auto load_batch = [&](int k0) {
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+      const bool kv = k0 + q < nchunks;
+      const float4* p = reinterpret_cast<const float4*>(a.part_o + (kv ? part_row(k0 + q) : 0) * D);
+#pragma unroll
+      for (int j = 0; j < NE; ++j) {
+        const int i = lane + 32 * j;
+        x[q][j] = kv && i < n4 ? __ldcg(p + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    }
+  };
+  auto weigh = [&](float (&f)[HPW], const float (&M)[HPW], float (&W)[HPW]) {
+#pragma unroll
+    for (int h = 0; h < HPW; ++h) {
+      f[h] = f[h] > -INFINITY ? fast_exp2(f[h] - M[h]) : 0.0f;
+      W[h] += warp_allreduce_sum(f[h]);
+    }
+  };
+  load_batch(0);  // in flight while the LSEs are read and reduced
+
+  float M[HPW], W[HPW], f[HPW];
+#pragma unroll
+  for (int h = 0; h < HPW; ++h) {
+    M[h] = -INFINITY;
+    W[h] = 0.0f;
+  }
+  for (int k0 = 0; k0 < nchunks; k0 += 32) {
+    load_lse(k0 + lane, f);
+#pragma unroll
+    for (int h = 0; h < HPW; ++h) M[h] = fmaxf(M[h], warp_allreduce_max(f[h]));
+  }
+  if (nchunks <= 32) weigh(f, M, W);  // f still holds the only round's LSEs
+  float4 o[NE];
+#pragma unroll
+  for (int j = 0; j < NE; ++j) o[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int k0 = 0; k0 < nchunks; k0 += 32) {
+    if (nchunks > 32) {
+      load_lse(k0 + lane, f);
+      weigh(f, M, W);
+    }
+    const int kn = min(32, nchunks - k0);
+    for (int kb = 0; kb < kn; kb += KB) {
+      if (k0 + kb > 0) load_batch(k0 + kb);
+#pragma unroll
+      for (int q = 0; q < KB; ++q) {
+        if (kb + q >= kn) break;
+#pragma unroll
+        for (int j = 0; j < NE; ++j) {
+          // Lane L's head in slot j is (L + 32j) / Q: at most two heads across the warp.
+          const int h_lo = (32 * j) / Q, h_hi = min(HPW - 1, (32 * j + 31) / Q);
+          const int h = (lane + 32 * j) / Q;
+          float w = 0.0f;
+#pragma unroll
+          for (int hh = h_lo; hh <= h_hi; ++hh) {
+            const float v = __shfl_sync(0xffffffffu, f[hh], kb + q);
+            if (h == hh) w = v;
+          }
+          o[j].x += w * x[q][j].x;
+          o[j].y += w * x[q][j].y;
+          o[j].z += w * x[q][j].z;
+          o[j].w += w * x[q][j].w;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NE; ++j) {
+    const int i = lane + 32 * j;
+    if (i >= n4) continue;
+    const int h_lo = (32 * j) / Q, h_hi = min(HPW - 1, (32 * j + 31) / Q);
+    const int h = i / Q;
+    float wsum = 0.0f;
+#pragma unroll
+    for (int hh = h_lo; hh <= h_hi; ++hh) {
+      if (h == hh) wsum = W[hh];
+    }
+    const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+    uint2 pk;
+    pk.x = Storage<T>::pack2(o[j].x * inv, o[j].y * inv);
+    pk.y = Storage<T>::pack2(o[j].z * inv, o[j].w * inv);
+    *reinterpret_cast<uint2*>(out_rows + static_cast<int64_t>(h) * D + 4 * (i - h * Q)) = pk;
+  }
+}
+
+// Picks the per-lane slot count for the group's nh x D outputs: 4, 8 or 16 float4 per lane
+// per chunk, with 4, 2 or 1 chunks' loads in flight (64 registers of loads in each case).
+template <typename T, int D, int HPW>
+__device__ __forceinline__ void merge_chunks(const DecodeArgs& a, const Seg& s, int slots_per_chunk, int mu, int nh,
+                                             T* out_rows, int lane) {
+  constexpr int Q = D / 4;
+  const int n4 = nh * Q;
+  if (n4 <= 128) {
+    merge_chunks_impl<T, D, HPW, 4, 4>(a, s, slots_per_chunk, mu, nh, out_rows, lane);
+  } else if (HPW * Q > 128 && n4 <= 256) {
+    merge_chunks_impl<T, D, HPW, (HPW * Q > 128 ? 8 : 4), 1>(a, s, slots_per_chunk, mu, nh, out_rows, lane);
+  } else if (HPW * Q > 256) {
+    merge_chunks_impl<T, D, HPW, (HPW * Q > 256 ? 16 : 4), 1>(a, s, slots_per_chunk, mu, nh, out_rows, lane);
+  }
+}
+
 // ------------------------------------------------------------------------- tensor-core kernel
 
 struct TcLayout {
@@ -338,9 +474,11 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   int* misc = reinterpret_cast<int*>(smem + L.misc);
   int* prefix = reinterpret_cast<int*>(smem + L.prefix);
   int* lens = reinterpret_cast<int*>(smem + L.lens);
-  // A stage half holds the tile as rows of 128 bytes, row r = (token * HT + head) * NCH + piece,
-  // in the TMA's 128-byte swizzle: 16-byte unit u of row r sits at unit u ^ (r & 7).
+  // A stage half holds the tile as rows of 128 bytes, row r = token * HT * NCH + piece with
+  // piece = head * NCH + c over the tile's HT heads, in the TMA's 128-byte swizzle: 16-byte unit
+  // u of row r sits at unit u ^ (r & 7).
   const int rows_per_tok = HT * NCH;
+  auto stage_row = [&](int tok, int piece) { return tok * rows_per_tok + piece; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -359,7 +497,13 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   volatile int* abort_flag = misc + 2;
 
   if (warp == kCW) {
-    // ---------------- producer warp: one 3-D TMA box per tensor per tile (per page for page size 8)
+    // ---------------- producer warp: one 3-D TMA box per tensor per tile (per page for page size 8).
+    // Lane-parallel issue for small stages: each pass finds how many of the next tiles have a
+    // free ring stage (lane t tests tile t's stage without blocking) and lane t issues tile t.
+    // One producer pass is a serial chain of ~1300 cycles, so one tile a pass caps an SM at a
+    // tile per ~0.66 us (12 GB/s with 8 KB tiles); batched, the ring fills at once at start-up
+    // and whenever consumers free several stages together. Only when the next stage is busy does
+    // the warp block, on that stage alone.
     Walk w;
     walk_init(a, misc, w);
     Seg s;
@@ -368,6 +512,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     const int p_rows = cfg.p_rows;
     const int nsub = kTile / p_rows;
     const uint32_t sub_bytes = 2u * p_rows * rows_per_tok * 128u;
+    // Batched issue pays off for small stages; with stages of 32 KB and more a tile takes
+    // longer to arrive than a producer pass, and single-tile passes measured faster.
+    const int batch_max = L.stage_bytes <= kBatchStageBytes ? min(32, nstage) : 1;
     bool ok = true;
     while (ok && walk_next(a, lens, prefix, w, s)) {
       const int ntok = s.tok_end - s.tok_begin;
@@ -376,63 +523,81 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.b) * a.bt_stride;
       const int last_page = (s.tok_end - 1) / a.page_size;
       const int piece0 = s.u * rows_per_tok;
-      // 32 consecutive block-table entries cached one per lane, the next 32 prefetched.
-      int cur_base = INT_MIN / 2, nxt_base = INT_MIN / 2;
-      int32_t cur = 0, nxt = 0;
-      for (int j = 0; j < ntiles; ++j, ++gt) {
-        const int stage = static_cast<int>(gt % nstage);
-        const uint32_t full = bars + 8u * stage;
-        const uint32_t empty = bars + 8u * (nstage + stage);
-        if (*abort_flag || !mbar_wait_bounded(empty, ((gt / nstage) & 1u) ^ 1u, a.sync, kWaitLimit)) {
-          *abort_flag = 1;
+      // Block-table window [wbase, wbase + 64): entry wbase + lane in cur, wbase + 32 + lane in nxt.
+      int wbase = s.tok_begin / a.page_size;
+      int32_t cur = wbase + lane <= last_page ? __ldg(bt_row + wbase + lane) : 0;
+      int32_t nxt = wbase + 32 + lane <= last_page ? __ldg(bt_row + wbase + 32 + lane) : 0;
+      int j0 = 0;
+      while (j0 < ntiles) {
+        if (*abort_flag) {
           ok = false;
           break;
         }
-        const int t0 = s.tok_begin + j * kTile;
-        bool v0 = false, v1 = false;
-        int y0 = 0, y1 = 0;
+        const int tok_first = s.tok_begin + j0 * kTile;
+        if (tok_first / a.page_size >= wbase + 32) {
+          wbase += 32;
+          cur = nxt;
+          nxt = wbase + 32 + lane <= last_page ? __ldg(bt_row + wbase + 32 + lane) : 0;
+        }
+        // Tiles whose pages all lie in the window (at least 16: page size >= 8, and the window
+        // reaches 32 pages past the first tile's page).
+        const int in_window = ((wbase + 64) * a.page_size - tok_first) / kTile;
+        const int want = min(min(ntiles - j0, batch_max), in_window);
+        // Lane t < want: the page(s) of tile j0 + t, looked up in the window by shuffles that
+        // every lane joins (other lanes look up a dummy entry). Done before any wait, so a
+        // freed stage is refilled with nothing but the copies' issue in between.
+        const int t0 = tok_first + lane * kTile;
+        bool v[2] = {false, false};
+        int y[2] = {0, 0};
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const int tok = t0 + r * p_rows;
-          if (r >= nsub || tok >= s.tok_end) break;
-          const int pidx = tok / a.page_size;
-          if (pidx < cur_base || pidx >= cur_base + 32) {
-            if (pidx == nxt_base) {
-              cur = nxt;
-              cur_base = nxt_base;
-            } else {
-              cur_base = pidx;
-              cur = pidx + lane <= last_page ? __ldg(bt_row + pidx + lane) : 0;
-            }
-            nxt_base = cur_base + 32;
-            nxt = nxt_base + lane <= last_page ? __ldg(bt_row + nxt_base + lane) : 0;
-          }
-          const int page = __shfl_sync(0xffffffffu, cur, pidx - cur_base);
+          const bool live = lane < want && r < nsub && tok < s.tok_end;
+          const int pidx = live ? tok / a.page_size : wbase;
+          const int src = pidx - wbase;
+          const int32_t from_cur = __shfl_sync(0xffffffffu, cur, src & 31);
+          const int32_t from_nxt = __shfl_sync(0xffffffffu, nxt, src & 31);
+          const int page = src < 32 ? from_cur : from_nxt;
           const bool good = page >= 0 && (a.num_pages < 0 || page < a.num_pages);
-          if (!good && lane == 0) atomicOr(a.sync, kStatusBadPage);
-          const int y = good ? page * a.page_size + (tok - pidx * a.page_size) : 0;
-          if (r == 0) {
-            v0 = good;
-            y0 = y;
-          } else {
-            v1 = good;
-            y1 = y;
-          }
+          if (live && !good) atomicOr(a.sync, kStatusBadPage);  // idempotent if looked up again
+          v[r] = live && good;
+          y[r] = v[r] ? page * a.page_size + (tok - pidx * a.page_size) : 0;
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(full, (v0 ? sub_bytes : 0u) + (v1 ? sub_bytes : 0u));
-          const uint32_t sbase = ring + stage * L.stage_bytes;
-          if (v0) {
-            tma_load_3d(sbase, &tmk, 0, piece0, y0, full, policy);
-            tma_load_3d(sbase + L.half, &tmv, 0, piece0, y0, full, policy);
+        const uint32_t g = gt + lane;
+        const uint32_t stage = g % static_cast<uint32_t>(nstage);
+        const bool is_free = lane < want && mbar_test_wait(bars + 8u * (nstage + stage), ((g / nstage) & 1u) ^ 1u);
+        const uint32_t freed = __ballot_sync(0xffffffffu, is_free);
+        int nb = freed == 0xffffffffu ? 32 : __ffs(~freed) - 1;  // leading free stages
+        // The CTA's first tile goes out alone, a pass ahead of the rest of the ring: at
+        // launch every SM requests its whole ring at once, and a first tile queued behind its
+        // siblings lands late and holds the consumers back (measured: ~1-2 us at batch 64).
+        if (gt == 0) nb = min(nb, 1);
+        if (nb == 0) {
+          const uint32_t e0 = bars + 8u * (nstage + gt % static_cast<uint32_t>(nstage));
+          if (!mbar_wait_bounded(e0, ((gt / nstage) & 1u) ^ 1u, a.sync, kWaitLimit)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
           }
-          if (v1) {
+          nb = 1;
+        }
+        if (lane < nb) {
+          const uint32_t full = bars + 8u * stage;
+          mbar_arrive_expect_tx(full, (v[0] ? sub_bytes : 0u) + (v[1] ? sub_bytes : 0u));
+          const uint32_t sbase = ring + stage * L.stage_bytes;
+          if (v[0]) {
+            tma_load_3d(sbase, &tmk, 0, piece0, y[0], full, policy);
+            tma_load_3d(sbase + L.half, &tmv, 0, piece0, y[0], full, policy);
+          }
+          if (v[1]) {
             const uint32_t off = p_rows * rows_per_tok * 128u;
-            tma_load_3d(sbase + off, &tmk, 0, piece0, y1, full, policy);
-            tma_load_3d(sbase + L.half + off, &tmv, 0, piece0, y1, full, policy);
+            tma_load_3d(sbase + off, &tmk, 0, piece0, y[1], full, policy);
+            tma_load_3d(sbase + L.half + off, &tmv, 0, piece0, y[1], full, policy);
           }
         }
         __syncwarp();
+        gt += nb;
+        j0 += nb;
       }
     }
     // Let every copy this CTA issued land before the CTA may exit.
@@ -451,7 +616,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   // lane's 16 contiguous bytes of a K row feed two k-steps. The output-row index of
   // O^T = V^T.P^T is permuted too: m-tile 4*c + mt, row g holds d = 64*c + 8*g + 2*mt and
   // row g+8 holds d + 1, so a lane reads one 16-byte unit of V per token and ends up owning
-  // 8 consecutive output values per head.
+  // 8 consecutive output values per head. Within a quarter-warp the K loads meet 2-way and
+  // the V loads 4-way shared-memory bank conflicts (every token of a (head, piece) has the
+  // same swizzle phase); a piece-major stage with permuted token rows removes them but measured
+  // no faster, the kernel being bound by HBM, not shared memory.
   zero_empty_sequences<T>(a, lens, threadIdx.x, kCW * 32);
   const int ht = warp % HT;
   const int hg = (warp / HT) % HG;
@@ -521,8 +689,8 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
-        const int ra = (g * HT + ht) * NCH + c;        // token g
-        const int rb = ((g + 8) * HT + ht) * NCH + c;  // token g + 8
+        const int ra = stage_row(g, ht * NCH + c);      // token g
+        const int rb = stage_row(g + 8, ht * NCH + c);  // token g + 8
 #pragma unroll
         for (int par = 0; par < 2; ++par) {
           const int u = par * 4 + t4;
@@ -584,7 +752,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const int tok = 2 * t4 + (q4 & 1) + 8 * (q4 >> 1);  // 2t4, 2t4+1, 2t4+8, 2t4+9
-          const int r = (tok * HT + ht) * NCH + c;
+          const int r = stage_row(tok, ht * NCH + c);
           v[q4] = lds128(sv + r * 128 + ((g ^ (r & 7)) << 4));
           if (tok >= valid) v[q4] = make_uint4(0u, 0u, 0u, 0u);
         }
@@ -710,8 +878,8 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       }
       continue;
     }
-    // This chunk's normalised partial and base-2 LSE, held in the fragment layout; padding
-    // heads of the last query-head group are never written nor read.
+    // This chunk's normalised partial and base-2 LSE, in the fragment layout; padding heads of
+    // the last query-head group are never written nor read.
     float lse_own[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -727,10 +895,13 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         }
       }
     }
+    // Few chunks: the last one merges from its registers (written only if it must publish).
+    // Many: every chunk writes its partial and the last merges them all with the flat merge.
+    const bool flat = s.nchunks > kRegisterMergeChunks;
     uint32_t* counter = counter_of(a, s.b, kvh, hg);
     const uint32_t siblings = static_cast<uint32_t>(s.nchunks - 1);
     bool last = __shfl_sync(0xffffffffu, published, 0) == siblings;
-    if (!last) {
+    if (flat || !last) {
       const int64_t slot = static_cast<int64_t>(s.chunk) * (HT * HG) + mu;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -750,100 +921,103 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           if (g == 0) a.part_lse[slot * HPW + hl] = lse_own[nt][e];
         }
       }
-      // Publish: the warp's stores are ordered before lane 0's fence by the warp barrier, and
-      // the fence orders them before the count.
+      // The warp barrier orders every lane's stores before what follows: the flat merge's
+      // reads by this warp, and lane 0's count (a release) otherwise.
       __syncwarp();
+    }
+    if (!last) {
       uint32_t before = 0;
-      if (lane == 0) {
-        __threadfence();
-        before = atomicAdd(counter, 1u);
-      }
+      if (lane == 0) before = atom_add_acq_rel_gpu(counter, 1u);  // publish; acquire if last
       last = __shfl_sync(0xffffffffu, before, 0) == siblings;
       if (!last) continue;
+    } else if (lane == 0) {
+      fence_acq_rel_gpu();  // acquire what the siblings published before the count was read
     }
-    // Last chunk: acquire the siblings' partials (fence after the observed count), then merge
-    // all chunks in chunk order with a running max, this chunk's own term taken from its
-    // registers (the values it would have stored), so the result does not depend on which
-    // chunk arrived last. A sibling's loads are all issued before any of its arithmetic.
-    if (lane == 0) __threadfence();
     __syncwarp();
-    float m_acc[NT][2], w_acc[NT][2], o_acc[KS][NT][4];
+    if (flat) {
+      merge_chunks<T, D, HPW>(a, s, HT * HG, mu, min(HPW, G - hg * HPW), out + out_row0 * D, lane);
+    } else {
+      // Merge in chunk order with a running max, this chunk's own term from its registers (the
+      // values it would have stored), so the result does not depend on which chunk merges; a
+      // sibling's loads are all issued before any of its arithmetic.
+      float m_acc[NT][2], w_acc[NT][2], o_acc[KS][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      m_acc[nt][0] = m_acc[nt][1] = -INFINITY;
-      w_acc[nt][0] = w_acc[nt][1] = 0.0f;
+      for (int nt = 0; nt < NT; ++nt) {
+        m_acc[nt][0] = m_acc[nt][1] = -INFINITY;
+        w_acc[nt][0] = w_acc[nt][1] = 0.0f;
 #pragma unroll
-      for (int mt = 0; mt < KS; ++mt) o_acc[mt][nt][0] = o_acc[mt][nt][1] = o_acc[mt][nt][2] = o_acc[mt][nt][3] = 0.0f;
-    }
-    for (int k = 0; k < s.nchunks; ++k) {
-      const int ck = chunk_id(a, s, k);
-      const bool own = ck == s.chunk;
-      const int64_t slot2 = static_cast<int64_t>(ck) * (HT * HG) + mu;
-      // Heads whose loads are in flight together: both of a lane's heads when registers allow.
-      constexpr int EG = NT * NCH <= 2 ? 2 : 1;
+        for (int mt = 0; mt < KS; ++mt) o_acc[mt][nt][0] = o_acc[mt][nt][1] = o_acc[mt][nt][2] = o_acc[mt][nt][3] = 0.0f;
+      }
+      for (int k = 0; k < s.nchunks; ++k) {
+        const int ck = chunk_id(a, s, k);
+        const bool own = ck == s.chunk;
+        const int64_t slot2 = static_cast<int64_t>(ck) * (HT * HG) + mu;
+        // Heads whose loads are in flight together: both of a lane's heads when registers allow.
+        constexpr int EG = NT * NCH <= 2 ? 2 : 1;
 #pragma unroll
-      for (int ne = 0; ne < NT * 2; ne += EG) {
-        const int nt = ne / 2;
-        float lse[EG];
-        float4 x[EG][NCH][2];
+        for (int ne = 0; ne < NT * 2; ne += EG) {
+          const int nt = ne / 2;
+          float lse[EG];
+          float4 x[EG][NCH][2];
 #pragma unroll
-        for (int ei = 0; ei < EG; ++ei) {
-          const int e = ne % 2 + ei;
-          const int hl = nt * 8 + 2 * t4 + e;
-          const bool ld = !own && hg * HPW + hl < G;
-          const float* po = a.part_o + (slot2 * HPW + hl) * D;
-          lse[ei] = own ? lse_own[nt][e] : ld ? __ldcg(a.part_lse + slot2 * HPW + hl) : -INFINITY;
+          for (int ei = 0; ei < EG; ++ei) {
+            const int e = ne % 2 + ei;
+            const int hl = nt * 8 + 2 * t4 + e;
+            const bool ld = !own && hg * HPW + hl < G;
+            const float* po = a.part_o + (slot2 * HPW + hl) * D;
+            lse[ei] = own ? lse_own[nt][e] : ld ? __ldcg(a.part_lse + slot2 * HPW + hl) : -INFINITY;
 #pragma unroll
-          for (int c = 0; c < NCH; ++c) {
+            for (int c = 0; c < NCH; ++c) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float* lo = &acc[c * 4 + 2 * h][nt][0];
-              const float* hi = &acc[c * 4 + 2 * h + 1][nt][0];
-              x[ei][c][h] = own ? make_float4(lo[e], lo[e + 2], hi[e], hi[e + 2])
-                          : ld  ? __ldcg(reinterpret_cast<const float4*>(po + c * 64 + 8 * g + 4 * h))
-                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+              for (int h = 0; h < 2; ++h) {
+                const float* lo = &acc[c * 4 + 2 * h][nt][0];
+                const float* hi = &acc[c * 4 + 2 * h + 1][nt][0];
+                x[ei][c][h] = own ? make_float4(lo[e], lo[e + 2], hi[e], hi[e + 2])
+                            : ld  ? __ldcg(reinterpret_cast<const float4*>(po + c * 64 + 8 * g + 4 * h))
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+              }
             }
           }
-        }
 #pragma unroll
-        for (int ei = 0; ei < EG; ++ei) {
-          const int e = ne % 2 + ei;
-          const float mn = fmaxf(m_acc[nt][e], lse[ei]);
-          if (mn == -INFINITY) continue;
-          const float fa = fast_exp2(m_acc[nt][e] - mn), fb = fast_exp2(lse[ei] - mn);
-          m_acc[nt][e] = mn;
-          w_acc[nt][e] = w_acc[nt][e] * fa + fb;
+          for (int ei = 0; ei < EG; ++ei) {
+            const int e = ne % 2 + ei;
+            const float mn = fmaxf(m_acc[nt][e], lse[ei]);
+            if (mn == -INFINITY) continue;
+            const float fa = fast_exp2(m_acc[nt][e] - mn), fb = fast_exp2(lse[ei] - mn);
+            m_acc[nt][e] = mn;
+            w_acc[nt][e] = w_acc[nt][e] * fa + fb;
 #pragma unroll
-          for (int c = 0; c < NCH; ++c) {
+            for (int c = 0; c < NCH; ++c) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float* lo = &o_acc[c * 4 + 2 * h][nt][0];
-              float* hi = &o_acc[c * 4 + 2 * h + 1][nt][0];
-              lo[e] = lo[e] * fa + fb * x[ei][c][h].x;
-              lo[e + 2] = lo[e + 2] * fa + fb * x[ei][c][h].y;
-              hi[e] = hi[e] * fa + fb * x[ei][c][h].z;
-              hi[e + 2] = hi[e + 2] * fa + fb * x[ei][c][h].w;
+              for (int h = 0; h < 2; ++h) {
+                float* lo = &o_acc[c * 4 + 2 * h][nt][0];
+                float* hi = &o_acc[c * 4 + 2 * h + 1][nt][0];
+                lo[e] = lo[e] * fa + fb * x[ei][c][h].x;
+                lo[e + 2] = lo[e + 2] * fa + fb * x[ei][c][h].y;
+                hi[e] = hi[e] * fa + fb * x[ei][c][h].z;
+                hi[e + 2] = hi[e + 2] * fa + fb * x[ei][c][h].w;
+              }
             }
           }
         }
       }
-    }
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+      for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int hl = nt * 8 + 2 * t4 + e;
-        if (hg * HPW + hl >= G) continue;
-        const float inv = w_acc[nt][e] > 0.0f ? 1.0f / w_acc[nt][e] : 0.0f;
-        T* orow = out + (out_row0 + hl) * D;
+        for (int e = 0; e < 2; ++e) {
+          const int hl = nt * 8 + 2 * t4 + e;
+          if (hg * HPW + hl >= G) continue;
+          const float inv = w_acc[nt][e] > 0.0f ? 1.0f / w_acc[nt][e] : 0.0f;
+          T* orow = out + (out_row0 + hl) * D;
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) {
-          uint4 pk;
-          pk.x = Storage<T>::pack2(o_acc[c * 4 + 0][nt][e] * inv, o_acc[c * 4 + 0][nt][e + 2] * inv);
-          pk.y = Storage<T>::pack2(o_acc[c * 4 + 1][nt][e] * inv, o_acc[c * 4 + 1][nt][e + 2] * inv);
-          pk.z = Storage<T>::pack2(o_acc[c * 4 + 2][nt][e] * inv, o_acc[c * 4 + 2][nt][e + 2] * inv);
-          pk.w = Storage<T>::pack2(o_acc[c * 4 + 3][nt][e] * inv, o_acc[c * 4 + 3][nt][e + 2] * inv);
-          *reinterpret_cast<uint4*>(orow + c * 64 + 8 * g) = pk;
+          for (int c = 0; c < NCH; ++c) {
+            uint4 pk;
+            pk.x = Storage<T>::pack2(o_acc[c * 4 + 0][nt][e] * inv, o_acc[c * 4 + 0][nt][e + 2] * inv);
+            pk.y = Storage<T>::pack2(o_acc[c * 4 + 1][nt][e] * inv, o_acc[c * 4 + 1][nt][e + 2] * inv);
+            pk.z = Storage<T>::pack2(o_acc[c * 4 + 2][nt][e] * inv, o_acc[c * 4 + 2][nt][e + 2] * inv);
+            pk.w = Storage<T>::pack2(o_acc[c * 4 + 3][nt][e] * inv, o_acc[c * 4 + 3][nt][e + 2] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 64 + 8 * g) = pk;
+          }
         }
       }
     }
@@ -1006,13 +1180,13 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
       a.part_o[(slot * G + h) * D + d] = l > 0.0f ? acc_s[idx] / l : 0.0f;
       if (d == 0) a.part_lse[slot * G + h] = l > 0.0f ? m_s[h] + __log2f(l) : -INFINITY;
     }
-    __threadfence();
+    // The block barrier orders every thread's stores before thread 0's count (a release);
+    // the count's acquire and the second barrier order the merge's reads after the siblings'.
     __syncthreads();
     uint32_t* counter = counter_of(a, s.b, kvh, 0);
-    if (tid == 0) misc[3] = atomicAdd(counter, 1u) == static_cast<uint32_t>(s.nchunks - 1);
+    if (tid == 0) misc[3] = atom_add_acq_rel_gpu(counter, 1u) == static_cast<uint32_t>(s.nchunks - 1);
     __syncthreads();
     if (misc[3]) {
-      __threadfence();
       for (int idx = tid; idx < G * D; idx += kGenThreads) {
         const int h = idx / D, d = idx - h * D;
         float M = -INFINITY;
@@ -1042,6 +1216,8 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
 
 namespace {
 
+constexpr int kMinTilesPerCta = 4;  // balanced plan: fewest tiles a CTA takes, by default
+
 struct Plan {
   bool tc = false;
   int D = 0, NT = 1;
@@ -1052,6 +1228,7 @@ struct Plan {
   int splits = 0, pps = 0;
   int slots = 0, slot_heads = 0;
   int seg_cost = 0;
+  int min_tiles = kMinTilesPerCta;
   size_t part_bytes = 0, sync_bytes = 0;
   const void* fn = nullptr;
 };
@@ -1106,7 +1283,6 @@ const void* gen_fn(int dtype) {
   }
 }
 
-constexpr int kMinTilesPerCta = 4;
 constexpr uint32_t kTcSmemBudget = 200 * 1024;  // one tensor-core CTA per SM
 constexpr int kMaxStages = 24;
 // Balanced plan: tiles' worth of time a tensor-core CTA loses per (sequence, head block) it
@@ -1116,7 +1292,8 @@ constexpr int kTcSegmentCost = 2;
 
 // Optional tuning overrides read once from the environment:
 //   KL_DECODE_HEADS_PER_TILE (1/2/4/8), KL_DECODE_STAGES (2..24), KL_DECODE_SEGMENT_COST
-//   (tiles charged per (sequence, unit) start by the balanced plan; negative: none). 0 = automatic.
+//   (tiles charged per (sequence, unit) start by the balanced plan; negative: none),
+//   KL_DECODE_MIN_TILES (fewest tiles a CTA of the balanced plan takes). 0 = automatic.
 int env_int(const char* name) {
   const char* v = std::getenv(name);
   return v ? std::atoi(v) : 0;
@@ -1214,6 +1391,8 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     chunks = 2LL * p.grid;
   }
   if (chunks * slots_per_chunk > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
+  const int forced_min = env_int("KL_DECODE_MIN_TILES");
+  if (forced_min > 0) p.min_tiles = std::min(forced_min, 1 << 20);
   const int forced_cost = env_int("KL_DECODE_SEGMENT_COST");
   p.seg_cost = forced_cost < 0 ? 0 : forced_cost > 0 ? std::min(forced_cost, 64) : p.tc ? kTcSegmentCost : 0;
   if (static_cast<int64_t>(batch) * (max_tiles + p.seg_cost) * p.units > INT_MAX / 2) {
@@ -1241,9 +1420,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   return g_encode;
 }
 
-// 3-D view of one cache: (64 elements = 128 bytes) x (Hkv*D/64 pieces of a token row, 128 B apart)
-// x (every token slot of the pool, Hkv*D*2 bytes apart). A box of HT*D/64 pieces x p_rows
-// tokens is one tile of a head block: for HT == Hkv a whole page, read front to back.
+// 3-D view of one cache: (64 elements = 128 bytes) x (Hkv*D/64 pieces of a token row, 128 B
+// apart) x (every token slot of the pool, Hkv*D*2 bytes apart). A box of HT*D/64 pieces x
+// p_rows tokens is one tile (or half of one, for page size 8) of a head block: for HT == Hkv a
+// whole page, read front to back.
 bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_tokens, int Hkv, int D, int HT,
                    int p_rows) {
   auto enc = encoder();
@@ -1329,7 +1509,7 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   a.units = p.units;
   a.splits = p.splits;
   a.pages_per_split = p.pps;
-  a.min_tiles = kMinTilesPerCta;
+  a.min_tiles = p.min_tiles;
   a.seg_cost = p.seg_cost;
   a.sync = static_cast<uint32_t*>(sync);
   a.part_o = static_cast<float*>(partials);
