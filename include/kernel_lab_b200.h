@@ -142,6 +142,25 @@ int kl_paged_decode_noalloc(int dtype, void* out, const void* q, const void* k_c
                             int num_kv_heads, int head_dim, int page_size, int64_t block_table_stride,
                             int max_pages_per_seq, int64_t num_pages, float scale, int num_splits, void* stream);
 
+/*
+ * Paged KV append: write each sequence's new token's K and V rows into its pages.
+ *   k_cache, v_cache    [num_pages, page_size, num_kv_heads, head_dim]   (NHD, contiguous)
+ *   k_new, v_new        [batch][num_kv_heads * head_dim], rows new_row_stride elements apart
+ *                       (a view of a fused QKV output needs no copy)
+ *   block_table         [batch, block_table_stride] int32, max_pages_per_seq entries used
+ *   positions           [batch] int32: token index written (the length before the append);
+ *                       negative = skip the sequence
+ * Token p of sequence b goes to page block_table[b, p / page_size], slot p % page_size. A
+ * position past max_pages_per_seq * page_size or a page id outside [0, num_pages) (num_pages < 0:
+ * unchecked) skips that sequence and ORs KL_STATUS_BAD_PAGE into *status (if non-null, a
+ * device word). Stream-ordered, no allocation. No counterpart in kernel-lab (its pools are
+ * built on the host); the layout is that of kernel-lab's csrc/kernel_lab.h:21-26.
+ */
+int kl_paged_kv_append(int dtype, void* k_cache, void* v_cache, const void* k_new, const void* v_new,
+                       const int32_t* block_table, const int32_t* positions, int batch, int num_kv_heads,
+                       int head_dim, int page_size, int64_t block_table_stride, int max_pages_per_seq,
+                       int64_t num_pages, int64_t new_row_stride, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

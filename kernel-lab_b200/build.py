@@ -33,7 +33,7 @@ OBJ_DIR = PKG_ROOT / "_build"
 LIB = OUT_DIR / "libkernel_lab_b200.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["rmsnorm.cu", "paged_decode.cu"]
+CU_SOURCES = ["rmsnorm.cu", "paged_decode.cu", "kv_append.cu"]
 HEADERS = [CSRC / "common.cuh", INCLUDE / "kernel_lab_b200.h"]
 
 

@@ -164,6 +164,50 @@ void paged_decode_attention_splits(at::Tensor& out, const at::Tensor& q, const a
   paged_decode_impl(out, q, k_cache, v_cache, block_table, seq_lens, scale, num_splits);
 }
 
+// Write each sequence's new token's K/V rows into its pages (kl_paged_kv_append); bad page
+// ids are skipped and flagged in the same status word as the decode calls of this stream.
+void paged_kv_append(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor& k_new, const at::Tensor& v_new,
+                     const at::Tensor& block_table, const at::Tensor& positions) {
+  TORCH_CHECK(k_cache.is_cuda() && v_cache.is_cuda() && k_new.is_cuda() && v_new.is_cuda(),
+              "tensors must be on CUDA");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous() &&
+                  k_cache.sizes() == v_cache.sizes(),
+              "caches are contiguous [num_pages, page_size, num_kv_heads, head_dim] of one shape");
+  const int64_t num_kv_heads = k_cache.size(2), head_dim = k_cache.size(3);
+  TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.strides() == v_new.strides(),
+              "k_new and v_new must have one shape and layout");
+  TORCH_CHECK((k_new.dim() == 3 && k_new.size(1) == num_kv_heads && k_new.size(2) == head_dim &&
+               k_new.stride(2) == 1 && k_new.stride(1) == head_dim) ||
+                  (k_new.dim() == 2 && k_new.size(1) == num_kv_heads * head_dim && k_new.stride(1) == 1),
+              "k_new is [batch, num_kv_heads, head_dim] (or [batch, num_kv_heads*head_dim]) with contiguous rows");
+  TORCH_CHECK(k_new.scalar_type() == k_cache.scalar_type() && v_new.scalar_type() == k_cache.scalar_type() &&
+                  v_cache.scalar_type() == k_cache.scalar_type(),
+              "new rows and caches must share a dtype");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && positions.scalar_type() == at::kInt,
+              "block_table and positions must be int32");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.stride(-1) == 1 && positions.is_contiguous(),
+              "block_table rows and positions must be contiguous");
+  const int64_t batch = k_new.size(0);
+  TORCH_CHECK(positions.numel() == batch && block_table.size(0) == batch,
+              "block_table and positions need one row / entry per sequence");
+  TORCH_CHECK(k_cache.device() == k_new.device() && v_cache.device() == k_new.device() &&
+                  v_new.device() == k_new.device() && block_table.device() == k_new.device() &&
+                  positions.device() == k_new.device(),
+              "tensors must be on one device");
+  if (batch == 0) return;
+  const c10::cuda::CUDAGuard guard(k_new.device());
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  Scratch& s = scratch_for(k_new.device(), stream, 0, 4);
+  check_status(kl_paged_kv_append(to_dtype(k_cache.scalar_type()), k_cache.data_ptr(), v_cache.data_ptr(),
+                                  k_new.data_ptr(), v_new.data_ptr(), block_table.data_ptr<int32_t>(),
+                                  positions.data_ptr<int32_t>(), static_cast<int>(batch),
+                                  static_cast<int>(num_kv_heads), static_cast<int>(head_dim),
+                                  static_cast<int>(k_cache.size(1)), block_table.stride(0),
+                                  static_cast<int>(block_table.size(1)), k_cache.size(0), k_new.stride(0),
+                                  static_cast<uint32_t*>(s.sync.data_ptr()), stream),
+               "paged_kv_append");
+}
+
 // Status bits (KL_STATUS_*) left by decode calls on the current device and stream.
 int64_t decode_status(bool clear) {
   const at::Device dev(at::kCUDA, c10::cuda::current_device());
@@ -186,6 +230,8 @@ void noop_decode(at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Te
                  const at::Tensor&, double) {}
 void noop_decode_splits(at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                         const at::Tensor&, double, int64_t) {}
+void noop_append(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                 const at::Tensor&) {}
 
 }  // namespace
 
@@ -198,6 +244,9 @@ TORCH_LIBRARY(kernel_lab, m) {
   m.def(
       "paged_decode_attention_splits(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, "
       "Tensor block_table, Tensor seq_lens, float scale, int num_splits) -> ()");
+  m.def(
+      "paged_kv_append(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, "
+      "Tensor block_table, Tensor positions) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(kernel_lab, CUDA, m) {
@@ -205,6 +254,7 @@ TORCH_LIBRARY_IMPL(kernel_lab, CUDA, m) {
   m.impl("fused_add_rms_norm", &fused_add_rms_norm);
   m.impl("paged_decode_attention", &paged_decode_attention);
   m.impl("paged_decode_attention_splits", &paged_decode_attention_splits);
+  m.impl("paged_kv_append", &paged_kv_append);
 }
 
 TORCH_LIBRARY_IMPL(kernel_lab, Meta, m) {
@@ -212,6 +262,7 @@ TORCH_LIBRARY_IMPL(kernel_lab, Meta, m) {
   m.impl("fused_add_rms_norm", &noop_fused);
   m.impl("paged_decode_attention", &noop_decode);
   m.impl("paged_decode_attention_splits", &noop_decode_splits);
+  m.impl("paged_kv_append", &noop_append);
 }
 
 // Importing kernel_lab._C runs the registrations above.

@@ -44,6 +44,11 @@ SIGNATURES = {
          _c_vp],
     ),
     "kl_paged_decode_read_status": (_c_int, [_c_vp, _c_u32p, _c_int, _c_vp]),
+    "kl_paged_kv_append": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int, _c_i64,
+         _c_i64, _c_vp, _c_vp],
+    ),
     "kl_paged_decode_noalloc": (
         _c_int,
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int,
@@ -207,4 +212,27 @@ def paged_decode_attention(
             _ptr(seq_lens), batch, hq, hkv, d, page, block_table.stride(0), scale, _stream(stream),
         ),
         "kl_paged_decode_attention",
+    )
+
+
+def paged_kv_append(
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    block_table: torch.Tensor,
+    positions: torch.Tensor,
+    status: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """kl_paged_kv_append on torch tensors; ``status`` is an optional int32/uint32 device word."""
+    batch = k_new.shape[0]
+    num_pages, page, hkv, d = k_cache.shape
+    _check(
+        load().kl_paged_kv_append(
+            DTYPE_CODES[k_cache.dtype], _ptr(k_cache), _ptr(v_cache), _ptr(k_new), _ptr(v_new), _ptr(block_table),
+            _ptr(positions), batch, hkv, d, page, block_table.stride(0), block_table.shape[1], num_pages,
+            k_new.stride(0), _ptr(status), _stream(stream),
+        ),
+        "kl_paged_kv_append",
     )

@@ -77,7 +77,23 @@ def paged_decode_attention(
     return out
 
 
+def paged_kv_append(
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    block_table: torch.Tensor,
+    positions: torch.Tensor,
+) -> None:
+    """Write each sequence's new token's K/V rows ([batch, num_kv_heads, head_dim], rows may be a
+    strided view) into its pages at token index ``positions[b]`` (in place; negative skips).
+    Page ids outside the pool are skipped and reported by :func:`decode_status`."""
+    _require()
+    torch.ops.kernel_lab.paged_kv_append(k_cache, v_cache, k_new, v_new, block_table, positions)
+
+
 def decode_status(clear: bool = False) -> int:
-    """KL_STATUS_* bits left by decode calls on the current device and stream (synchronises)."""
+    """KL_STATUS_* bits left by decode and append calls on the current device and stream
+    (synchronises)."""
     _require()
     return int(_C.decode_status(clear))

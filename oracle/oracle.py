@@ -122,6 +122,46 @@ def paged_decode_attention(
     return round_to(out, dtype)
 
 
+KL_STATUS_BAD_PAGE = 1
+
+
+def paged_kv_append(
+    k_cache: np.ndarray,
+    v_cache: np.ndarray,
+    k_new: np.ndarray,
+    v_new: np.ndarray,
+    block_table: np.ndarray,
+    positions: np.ndarray,
+    max_pages: int | None = None,
+) -> tuple[np.ndarray, np.ndarray, int]:
+    """Write token ``positions[b]`` of every sequence into its page of the NHD pool.
+
+    The pool layout is kernel-lab's (csrc/kernel_lab.h:21-26: ``[num_pages, page_size,
+    num_kv_heads, head_dim]``): token t of sequence b lives at page ``block_table[b, t // P]``,
+    slot ``t % P``, which is how kernel-lab's fixtures fill it (kernel_lab/kv_cache.py:66-72)
+    and how its decode reads it (csrc/paged_attention.cu:68-70). kernel-lab has no append op;
+    this restates that layout as a scatter. Negative positions skip their sequence; a position
+    past ``max_pages * P`` or a page id outside the pool skips it and sets the bad-page bit.
+    Returns new caches (the inputs are not modified) and the status bits.
+    """
+    k = np.array(k_cache, copy=True)
+    v = np.array(v_cache, copy=True)
+    num_pages, page_size = k.shape[0], k.shape[1]
+    width = block_table.shape[1] if max_pages is None else max_pages
+    status = 0
+    for b, pos in enumerate(np.asarray(positions).tolist()):
+        if pos < 0:
+            continue
+        pidx = pos // page_size
+        page = int(block_table[b, pidx]) if pidx < width else -1
+        if page < 0 or page >= num_pages:
+            status |= KL_STATUS_BAD_PAGE
+            continue
+        k[page, pos % page_size] = np.asarray(k_new[b]).reshape(k.shape[2:])
+        v[page, pos % page_size] = np.asarray(v_new[b]).reshape(v.shape[2:])
+    return k, v, status
+
+
 def decode_bytes(seq_lens, num_q_heads: int, num_kv_heads: int, head_dim: int, elem_bytes: int) -> int:
     """Algorithmic HBM bytes of one decode call: K and V read once, q read and out written once.
 

@@ -37,6 +37,7 @@ def test_header_declares_the_abi():
         "kl_paged_decode_attention",
         "kl_paged_decode_read_status",
         "kl_paged_decode_noalloc",
+        "kl_paged_kv_append",
     ]
 
 
@@ -76,6 +77,14 @@ def test_noop_and_validation_without_a_device():
     size = ctypes.c_size_t(1)
     assert lib.kl_paged_decode_workspace_size(2, 0, 32, 8, 128, 16, 4, 0, ctypes.byref(size), ctypes.byref(size)) == 0
     assert lib.kl_paged_decode_read_status(None, None, 0, None) == CUDA_ERROR_INVALID_VALUE
+    # Append: batch 0 is a no-op; missing buffers or a row stride shorter than a row are rejected.
+    assert lib.kl_paged_kv_append(2, *([None] * 6), 0, 8, 128, 16, 4, 4, 10, 1024, None, None) == 0
+    assert lib.kl_paged_kv_append(2, *([None] * 6), 4, 8, 128, 16, 4, 4, 10, 1024, None, None) == (
+        CUDA_ERROR_INVALID_VALUE
+    )
+    assert lib.kl_paged_kv_append(2, *([1] * 6), 4, 8, 128, 16, 4, 4, 10, 1000, None, None) == (
+        CUDA_ERROR_INVALID_VALUE
+    )
 
 
 # kernel-lab's schema strings, verbatim (csrc/torch_bindings.cpp:108-113 there).
@@ -96,6 +105,9 @@ def test_torch_ops_have_the_reference_schemas():
         op = getattr(torch.ops.kernel_lab, name)
         assert str(op.default._schema) == str(torch._C.parse_schema("kernel_lab::" + schema))
     assert "num_splits" in str(torch.ops.kernel_lab.paged_decode_attention_splits.default._schema)
+    assert str(torch.ops.kernel_lab.paged_kv_append.default._schema) == str(torch._C.parse_schema(
+        "kernel_lab::paged_kv_append(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, "
+        "Tensor block_table, Tensor positions) -> ()"))
     assert cuda_ops._LOADED
 
 
@@ -112,6 +124,8 @@ def test_meta_kernels_trace_without_a_device():
     bt = torch.empty(2, 2, device="meta", dtype=torch.int32)
     ln = torch.empty(2, device="meta", dtype=torch.int32)
     torch.ops.kernel_lab.paged_decode_attention(torch.empty_like(q), q, kc, kc, bt, ln, 0.125)
+    kn = torch.empty(2, 2, 64, device="meta", dtype=torch.bfloat16)
+    torch.ops.kernel_lab.paged_kv_append(kc, torch.empty_like(kc), kn, kn, bt, ln)
 
 
 def test_cuda_ops_fail_loudly_without_a_device():

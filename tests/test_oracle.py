@@ -137,3 +137,36 @@ def test_decode_bytes_model():
     assert oracle.decode_bytes([10, 20], 4, 2, 8, 2) == 2 * 30 * 2 * 8 * 2 + 2 * 2 * 4 * 8 * 2
     # Config 3 headline: batch 64, context 4096, Llama-3-8B heads, bf16.
     assert oracle.decode_bytes([4096] * 64, 32, 8, 128, 2) == 1_074_790_400
+
+
+def test_append_oracle_rebuilds_the_fixture_pool_token_by_token():
+    """Appending every token of every sequence, in order, through the append oracle fills the
+    same pages as kernel-lab's fixture builder (kv_cache.py:33-80, restated in this package's
+    build_paged_kv); spare pages are untouched, bad pages and padding are reported / skipped."""
+    import torch
+
+    from kernel_lab.kv_cache import build_paged_kv, pages_for
+
+    lens = [1, 15, 16, 17, 40]
+    keys = [torch.randn(n, 2, 8) for n in lens]
+    values = [torch.randn(n, 2, 8) for n in lens]
+    kv = build_paged_kv(keys, values, page_size=16, poison=0.0)
+    k = np.zeros_like(kv.k_cache.numpy())
+    v = np.zeros_like(kv.v_cache.numpy())
+    bt = kv.block_table.numpy()
+    for t in range(max(lens)):
+        pos = np.array([t if t < n else -1 for n in lens], np.int32)
+        kn = np.stack([keys[b][min(t, n - 1)].numpy() for b, n in enumerate(lens)])
+        vn = np.stack([values[b][min(t, n - 1)].numpy() for b, n in enumerate(lens)])
+        k, v, status = oracle.paged_kv_append(k, v, kn, vn, bt, pos)
+        assert status == 0
+    np.testing.assert_array_equal(k, kv.k_cache.numpy())
+    np.testing.assert_array_equal(v, kv.v_cache.numpy())
+    assert [pages_for(n, 16) for n in lens] == [1, 1, 1, 2, 3]
+
+    bad = bt.copy()
+    bad[0, 0] = kv.num_pages  # out of the pool
+    k2, _, status = oracle.paged_kv_append(k, v, np.ones((5, 2, 8), np.float32), np.ones((5, 2, 8), np.float32), bad,
+                                           np.array([0, -1, -1, -1, 16 * bt.shape[1]], np.int32))
+    assert status == oracle.KL_STATUS_BAD_PAGE
+    np.testing.assert_array_equal(k2, k)  # both writes skipped
