@@ -8,11 +8,12 @@ For N > 1 launch one process per GPU:
 
 Workload (default ``decode``): kernel-lab's headline, paged decode attention with Llama-3-8B
 heads (32 query / 8 KV, head_dim 128, 16-token pages), bf16, batch 64, context 4096,
-shuffled pages, NaN-poisoned spare pages. A step is one decode call. At N GPUs the KV
-heads are sharded N ways (tensor parallel) and the batch grows to 64*N, so every GPU
-streams the same 1.07 GB of KV per step (weak scaling); the per-head outputs are
-all-gathered with NCCL inside the step. ``decode70b``: Llama-3-70B heads (64/8), batch
-256, context 8192, total work fixed across N (strong scaling). ``rmsnorm``: fused add +
+shuffled pages, NaN-poisoned spare pages. A step is one decode call. At N GPUs the batch
+grows to 64*N and every rank decodes its own 64 sequences with every head: sequences are
+independent, so there is no collective, and every GPU streams the same 1.07 GB of KV per
+step (weak scaling). ``decode70b``: Llama-3-70B heads (64/8), batch 256, context 8192,
+total work fixed across N (strong scaling) in the tensor-parallel layout: KV heads sharded
+N ways and the outputs all-gathered with NCCL inside the step. ``rmsnorm``: fused add +
 RMSNorm, 4096 x 8192 bf16.
 
 One JSON line on rank 0: value = aggregate algorithmic HBM GB/s (K+V read once, q and
@@ -59,10 +60,14 @@ def parse() -> argparse.Namespace:
 
 def workload_spec(name: str, world: int) -> dict:
     if name == "decode":
+        # Sequences are independent: each rank decodes its own 64 with every head, no collective.
         return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
+                    layout="sequences",
                     desc="paged decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU, ctx 4096")
     if name == "decode70b":
+        # Tensor-parallel layout: KV heads sharded, one all-gather of the outputs per step.
         return dict(kind="decode", batch=256, ctx=8192, hq=64, hkv=8, d=128, page=16, scaling="strong",
+                    layout="kv_heads",
                     desc="paged decode, Llama-3-70B heads 64/8/128, page 16, bf16, batch 256, ctx 8192")
     return dict(kind="rmsnorm", rows=4096, hidden=8192, scaling="weak",
                 desc="fused residual-add + RMSNorm, 4096 x 8192 bf16, eps 1e-5")
@@ -274,17 +279,25 @@ def main() -> None:
 
     if spec["kind"] == "decode":
         from kernel_lab.kv_cache import random_paged_pool
-        from kernel_lab.sharding import gather_heads, kv_head_range
+        from kernel_lab.sharding import batch_range, gather_heads, kv_head_range
 
         B, ctx, hq, hkv, d, page = (spec[k] for k in ("batch", "ctx", "hq", "hkv", "d", "page"))
-        lo, hi = kv_head_range(hkv, world, rank)
-        q, kv = random_paged_pool([ctx] * B, hq, hkv, d, page, dtype=torch.bfloat16, device=dev, seed=1234,
-                                  kv_head_slice=(lo, hi))
-        hq_l, hkv_l = q.shape[1], hi - lo
+        gather = spec["layout"] == "kv_heads" and world > 1
+        if spec["layout"] == "kv_heads":
+            lo, hi = kv_head_range(hkv, world, rank)
+            b_local = B
+            q, kv = random_paged_pool([ctx] * B, hq, hkv, d, page, dtype=torch.bfloat16, device=dev, seed=1234,
+                                      kv_head_slice=(lo, hi))
+        else:
+            b_lo, b_hi = batch_range(B, world, rank)
+            b_local = b_hi - b_lo
+            q, kv = random_paged_pool([ctx] * b_local, hq, hkv, d, page, dtype=torch.bfloat16, device=dev,
+                                      seed=1234 + rank)
+        hq_l, hkv_l = q.shape[1], kv.k_cache.shape[2]
         scale = d**-0.5
         out_local = torch.empty_like(q)
-        out_full = torch.empty((B, hq, d), dtype=q.dtype, device=dev)
-        kernel_work = decode_attention_work([ctx] * B, hq_l, hkv_l, d, 2)  # per rank, per launch
+        out_full = torch.empty((B, hq, d), dtype=q.dtype, device=dev) if gather else None
+        kernel_work = decode_attention_work([ctx] * b_local, hq_l, hkv_l, d, 2)  # per rank, per launch
         job_bytes = decode_attention_work([ctx] * B, hq, hkv, d, 2).bytes
 
         def kernel():
@@ -293,7 +306,7 @@ def main() -> None:
 
         def step():
             kernel()
-            if world > 1:
+            if gather:
                 gather_heads(out_local, world, out=out_full)
 
         metric = METRIC
@@ -323,7 +336,7 @@ def main() -> None:
     # step is exactly one launch of the kernel, so the region's two events give the kernel's
     # average launch duration (an event between back-to-back launches would add ~5 us of
     # launch gap to every step); with a gather in the step, events bracket each kernel too.
-    per_kernel = world > 1 and spec["kind"] == "decode"
+    per_kernel = spec["kind"] == "decode" and gather
     n_ev = args.steps if per_kernel else 0
     k_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     k_end = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
@@ -363,11 +376,11 @@ def main() -> None:
         q_h = q.cpu().pin_memory()
         bt_h = kv.block_table.cpu().pin_memory()
         ln_h = kv.seq_lens.cpu().pin_memory()
-        out_shape = out_full.shape if world > 1 else out_local.shape
+        out_shape = out_full.shape if gather else out_local.shape
         out_hs = [torch.empty(out_shape, dtype=q.dtype).pin_memory() for _ in range(2)]
         slots = [dict(q=torch.empty_like(q), bt=torch.empty_like(kv.block_table), ln=torch.empty_like(kv.seq_lens),
                       out=torch.empty_like(out_local),
-                      full=torch.empty(out_shape, dtype=q.dtype, device=dev) if world > 1 else None,
+                      full=torch.empty(out_shape, dtype=q.dtype, device=dev) if gather else None,
                       inputs_free=None, out_read=None) for _ in range(2)]
         s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
         h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + ln_h.numel() * 4
@@ -391,7 +404,7 @@ def main() -> None:
                 stream.wait_event(sl["out_read"])  # the copy-out two steps back has read the slot
             torch.ops.kernel_lab.paged_decode_attention(sl["out"], sl["q"], kv.k_cache, kv.v_cache, sl["bt"],
                                                         sl["ln"], scale)
-            src = sl["out"] if world == 1 else gather_heads(sl["out"], world, out=sl["full"])
+            src = gather_heads(sl["out"], world, out=sl["full"]) if gather else sl["out"]
             done = torch.cuda.Event()
             done.record(stream)
             sl["inputs_free"] = done
@@ -446,11 +459,11 @@ def main() -> None:
     if spec["kind"] == "decode":
         # The pipelined steps computed what the resident steps did (same inputs, deterministic
         # kernel): a copy that raced its slot would show here.
-        ref = (out_full if world > 1 else out_local).cpu()
+        ref = (out_full if gather else out_local).cpu()
         if not torch.equal(out_hs[(e2e_count[0] - 1) % 2], ref):
             raise SystemExit("e2e output differs from the device-resident step's output")
     e2e = {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d * world),
-           "d2h_bytes_per_step": int(d2h * (1 if spec["kind"] == "decode" else world)), "ms_per_step": e2e_ms}
+           "d2h_bytes_per_step": int(d2h * world), "ms_per_step": e2e_ms}
 
     status = cuda_ops.decode_status(clear=True) if spec["kind"] == "decode" else 0
 
@@ -462,7 +475,9 @@ def main() -> None:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_measure(spec["kind"], spec, args.cpu_seconds)
-        cfg = {"workload": spec["desc"], "l2": L2_NOTE, "parallelism": f"kv-head tp{world}" if world > 1 else "1 gpu"}
+        layout = spec.get("layout")
+        parallelism = "1 gpu" if world == 1 else f"kv-head tp{world}" if layout == "kv_heads" else f"sequences dp{world}"
+        cfg = {"workload": spec["desc"], "l2": L2_NOTE, "parallelism": parallelism}
         if spec["kind"] == "decode":
             cfg.update(batch=spec["batch"], ctx=spec["ctx"], num_q_heads=spec["hq"], num_kv_heads=spec["hkv"],
                        head_dim=spec["d"], page_size=spec["page"], pool_pages=int(kv.k_cache.shape[0]),

@@ -61,7 +61,7 @@
 namespace klb {
 
 constexpr int kTile = 16;
-constexpr uint32_t kBatchStageBytes = 16 * 1024;  // producer issues tiles in batches up to this stage size
+constexpr uint32_t kBatchStageBytes = 32 * 1024;  // producer issues tiles in batches up to this stage size
 constexpr int kRegisterMergeChunks = 4;  // splits of at most this many chunks merge from registers         // tokens per tile: the MMA's M
 constexpr int kCW = 8;            // consumer warps of the tensor-core kernel
 constexpr int kTCThreads = 32 * (kCW + 1);
@@ -437,7 +437,8 @@ __host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int
   off += nstage * L.stage_bytes;
   L.bars = off;
   off += 2u * nstage * 8u;
-  const uint32_t red_warps = TW > 1 ? kCW : 0;
+  // Combine slots for the warps that hand their (m, l, acc) to a tw == 0 warp: all but kCW / TW.
+  const uint32_t red_warps = TW > 1 ? kCW - kCW / TW : 0;
   L.red_m = off;
   off += red_warps * 8u * NT * 4u;
   L.red_l = off;
@@ -512,8 +513,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     const int p_rows = cfg.p_rows;
     const int nsub = kTile / p_rows;
     const uint32_t sub_bytes = 2u * p_rows * rows_per_tok * 128u;
-    // Batched issue pays off for small stages; with stages of 32 KB and more a tile takes
-    // longer to arrive than a producer pass, and single-tile passes measured faster.
+    // Batched issue pays off for stages up to 32 KB (4 heads or fewer per tile); with 64 KB
+    // stages a tile takes longer to arrive than a producer pass, and single-tile passes
+    // measured faster (batch 256 x 8192 tokens, 70B heads).
     const int batch_max = L.stage_bytes <= kBatchStageBytes ? min(32, nstage) : 1;
     bool ok = true;
     while (ok && walk_next(a, lens, prefix, w, s)) {
@@ -793,9 +795,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     // Warps that split the tiles of one (head, group) combine into the tw == 0 warp.
     if (TW > 1) {
       if (tw != 0) {
-        float* rm = red_m + warp * HPW;
-        float* rl = red_l + warp * HPW;
-        float* ra = red_acc + warp * HPW * (D + 4);
+        const int slot_w = warp - HT * HG;  // warps with tw >= 1, in order
+        float* rm = red_m + slot_w * HPW;
+        float* rl = red_l + slot_w * HPW;
+        float* ra = red_acc + slot_w * HPW * (D + 4);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -822,7 +825,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           for (int e = 0; e < 2; ++e) {
             const int hl = nt * 8 + 2 * t4 + e;
             float M = m_run[nt][e];
-            for (int t2 = 1; t2 < TW; ++t2) M = fmaxf(M, red_m[(mu + HT * HG * t2) * HPW + hl]);
+            for (int t2 = 1; t2 < TW; ++t2) M = fmaxf(M, red_m[(mu + HT * HG * (t2 - 1)) * HPW + hl]);
             if (M == -INFINITY) continue;
             const float f0 = fast_exp2(m_run[nt][e] - M);
             float l = l_run[nt][e] * f0;
@@ -832,7 +835,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
               acc[mt][nt][2 + e] *= f0;
             }
             for (int t2 = 1; t2 < TW; ++t2) {
-              const int w2 = mu + HT * HG * t2;
+              const int w2 = mu + HT * HG * (t2 - 1);  // combine slot of warp (ht, hg, t2)
               const float m2 = red_m[w2 * HPW + hl];
               if (m2 == -INFINITY) continue;
               const float f = fast_exp2(m2 - M);
@@ -1283,7 +1286,7 @@ const void* gen_fn(int dtype) {
   }
 }
 
-constexpr uint32_t kTcSmemBudget = 200 * 1024;  // one tensor-core CTA per SM
+constexpr uint32_t kTcSmemBudget = 225 * 1024;  // one tensor-core CTA per SM (227 KB is the limit)
 constexpr int kMaxStages = 24;
 // Balanced plan: tiles' worth of time a tensor-core CTA loses per (sequence, head block) it
 // starts (Q loads, partial write and count). Measured at batch 64 x 4096 tokens: charging 2

@@ -1,4 +1,7 @@
-"""Tensor-parallel decode attention by KV head (one process per GPU, NCCL over NVLink).
+"""Multi-GPU layouts of decode attention (one process per GPU, NCCL over NVLink).
+
+By sequence (``batch_range``): sequences are independent, so each rank decodes its own and
+nothing is exchanged. By KV head (tensor parallel, below):
 
 A KV head and the query heads of its group need no data from any other head, so the
 heads shard with no exchange during the attention itself: rank r of N keeps KV heads
@@ -28,6 +31,16 @@ def kv_head_range(num_kv_heads: int, world_size: int, rank: int) -> tuple[int, i
     return rank * per, (rank + 1) * per
 
 
+def batch_range(batch: int, world_size: int, rank: int) -> tuple[int, int]:
+    """Sequences [lo, hi) decoded by `rank` when the batch is split instead of the heads
+    (sequences are independent: no collective). Uneven batches give the first ranks one more."""
+    if world_size <= 0 or not 0 <= rank < world_size or batch < 0:
+        raise ValueError(f"bad rank {rank} of {world_size} for batch {batch}")
+    per, extra = divmod(batch, world_size)
+    lo = rank * per + min(rank, extra)
+    return lo, lo + per + (1 if rank < extra else 0)
+
+
 def shard_heads(
     q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, world_size: int, rank: int
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
@@ -42,21 +55,30 @@ def shard_heads(
     )
 
 
+_GATHER_BUFFERS: dict[tuple, torch.Tensor] = {}
+
+
 def gather_heads(local_out: torch.Tensor, world_size: int, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """All-gather per-rank outputs [B, Hq/N, D] and return the full [B, Hq, D] in head order."""
+    """All-gather per-rank outputs [B, Hq/N, D] and return the full [B, Hq, D] in head order.
+
+    The collective lands in a cached [N, B, Hq/N, D] buffer (one per shape, device and group);
+    one permuting copy then writes `out` (allocated if not given)."""
     if world_size == 1:
         if out is not None:
             out.copy_(local_out)
             return out
         return local_out
     b, hl, d = local_out.shape
-    stacked = torch.empty((world_size * b, hl, d), dtype=local_out.dtype, device=local_out.device)
+    key = (world_size, b, hl, d, local_out.dtype, local_out.device, id(group))
+    stacked = _GATHER_BUFFERS.get(key)
+    if stacked is None:
+        stacked = torch.empty((world_size * b, hl, d), dtype=local_out.dtype, device=local_out.device)
+        _GATHER_BUFFERS[key] = stacked
     dist.all_gather_into_tensor(stacked, local_out.contiguous(), group=group)
-    full = stacked.view(world_size, b, hl, d).permute(1, 0, 2, 3).reshape(b, world_size * hl, d)
-    if out is not None:
-        out.copy_(full)
-        return out
-    return full
+    if out is None:
+        out = torch.empty((b, world_size * hl, d), dtype=local_out.dtype, device=local_out.device)
+    out.view(b, world_size, hl, d).copy_(stacked.view(world_size, b, hl, d).permute(1, 0, 2, 3))
+    return out
 
 
 class ShardedPagedDecode:

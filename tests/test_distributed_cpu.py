@@ -116,6 +116,10 @@ def test_head_ranges_and_shards_cover_the_problem():
     from kernel_lab.sharding import gather_heads, kv_head_range, shard_heads
 
     assert [kv_head_range(8, 4, r) for r in range(4)] == [(0, 2), (2, 4), (4, 6), (6, 8)]
+    from kernel_lab.sharding import batch_range
+
+    assert [batch_range(10, 4, r) for r in range(4)] == [(0, 3), (3, 6), (6, 8), (8, 10)]
+    assert [batch_range(128, 2, r) for r in range(2)] == [(0, 64), (64, 128)]
     try:
         kv_head_range(8, 3, 0)
         raise AssertionError("uneven sharding must be rejected")
