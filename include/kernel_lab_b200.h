@@ -161,6 +161,35 @@ int kl_paged_kv_append(int dtype, void* k_cache, void* v_cache, const void* k_ne
                        int head_dim, int page_size, int64_t block_table_stride, int max_pages_per_seq,
                        int64_t num_pages, int64_t new_row_stride, uint32_t* status, void* stream);
 
+/*
+ * FP8 KV cache (the roadmap item of kernel-lab's README.md:98): k_cache / v_cache hold e4m3
+ * codes (one byte per element, same NHD layout), dequantised as code value * k_scale[h] (or
+ * v_scale[h]) for KV head h; k_scale, v_scale are [num_kv_heads] fp32 device arrays. q and out
+ * are fp16 or bf16 (dtype). Otherwise exactly kl_paged_decode, including the scratch from
+ * kl_paged_decode_workspace_size (same dtype and shape arguments). head_dim 128 or 256, page
+ * size 8 or a multiple of 16; other shapes return cudaErrorInvalidValue. The MMAs run in f16
+ * (e4m3 -> f16 is exact; q is rounded to f16, probabilities to f16), accumulating in fp32.
+ * No counterpart in kernel-lab.
+ */
+int kl_paged_decode_fp8(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                        const float* k_scale, const float* v_scale, const int32_t* block_table,
+                        const int32_t* seq_lens, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                        int page_size, int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
+                        float scale, int num_splits, void* partials, size_t partial_bytes, void* sync,
+                        size_t sync_bytes, void* stream);
+
+/*
+ * kl_paged_kv_append into an e4m3 cache: each new row (dtype fp32, fp16 or bf16) is quantised
+ * per KV head as e4m3(x / scale[h]) (float32 division, round to nearest-even, saturating to
+ * +-448; NaN stays NaN) and written like kl_paged_kv_append. head_dim must be even.
+ * No counterpart in kernel-lab.
+ */
+int kl_paged_kv_append_fp8(int dtype, void* k_cache, void* v_cache, const void* k_new, const void* v_new,
+                           const float* k_scale, const float* v_scale, const int32_t* block_table,
+                           const int32_t* positions, int batch, int num_kv_heads, int head_dim, int page_size,
+                           int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
+                           int64_t new_row_stride, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

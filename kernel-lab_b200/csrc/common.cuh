@@ -11,6 +11,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 namespace klb {
 
@@ -57,6 +58,22 @@ template <typename T, int N>
 struct alignas(sizeof(T) * N) Vec {
   T v[N];
 };
+
+// Two e4m3 values (low byte first) -> f16x2 (low half first); exact, e4m3 being a subset of f16.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xffffu), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
+// A packed pair of the storage type -> f16x2 (the operand type of the fp8-cache MMAs).
+template <typename T>
+__device__ __forceinline__ uint32_t to_f16x2(uint32_t v);
+template <>
+__device__ __forceinline__ uint32_t to_f16x2<__half>(uint32_t v) { return v; }
+template <>
+__device__ __forceinline__ uint32_t to_f16x2<__nv_bfloat16>(uint32_t v) {
+  return Storage<__half>::pack2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
 
 // ----------------------------------------------------------------- reductions
 

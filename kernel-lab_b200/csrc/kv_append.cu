@@ -1,5 +1,5 @@
-// Paged KV append for sm_100a: the write side of the paged cache. Each sequence's new
-// token's K and V rows go into its page pool at token position positions[b]:
+// Paged KV append for sm_100a: the write side of the paged cache (16-bit and e4m3 caches).
+// Each sequence's new token's K and V rows go into its page pool at token position positions[b]:
 //   page = block_table[b, pos / page_size], slot = pos % page_size,
 //   k_cache[page, slot, :, :] = k_new[b], v_cache[page, slot, :, :] = v_new[b]
 // in kernel-lab's NHD layout (csrc/kernel_lab.h:21-26: [num_pages, page_size, num_kv_heads,
@@ -93,6 +93,36 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_scalar(const AppendA
   }
 }
 
+// e4m3 cache: each new row is quantised per KV head, e4m3(x / scale) with an IEEE float
+// division, rounding to nearest-even and saturating to +-448 (NaN stays NaN).
+template <typename E>
+__global__ void __launch_bounds__(kAppendThreads) kv_append_e4m3(const AppendArgs a, const float* k_scale,
+                                                                  const float* v_scale, int head_dim) {
+  const int b = blockIdx.x;
+  const int pos = a.positions[b];
+  if (pos < 0) return;
+  const int pidx = pos / a.page_size;
+  int64_t page = -1;
+  if (pidx < a.max_pages) page = a.block_table[static_cast<int64_t>(b) * a.bt_stride + pidx];
+  if (page < 0 || (a.num_pages >= 0 && page >= a.num_pages)) {
+    if (threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusBadPage);
+    return;
+  }
+  const int64_t dst_row = page * a.page_size + (pos - pidx * a.page_size);
+  const E* ks = static_cast<const E*>(a.k_new) + static_cast<int64_t>(b) * a.new_stride;
+  const E* vs = static_cast<const E*>(a.v_new) + static_cast<int64_t>(b) * a.new_stride;
+  uint8_t* kd = static_cast<uint8_t*>(a.k_cache) + dst_row * a.row_elems;
+  uint8_t* vd = static_cast<uint8_t*>(a.v_cache) + dst_row * a.row_elems;
+  for (int i = 2 * threadIdx.x; i < a.row_elems; i += 2 * blockDim.x) {  // head_dim is even
+    const int h = i / head_dim;
+    const float kq = k_scale[h], vq = v_scale[h];
+    const float2 kx = make_float2(Storage<E>::load(ks[i]) / kq, Storage<E>::load(ks[i + 1]) / kq);
+    const float2 vx = make_float2(Storage<E>::load(vs[i]) / vq, Storage<E>::load(vs[i + 1]) / vq);
+    *reinterpret_cast<__nv_fp8x2_storage_t*>(kd + i) = __nv_cvt_float2_to_fp8x2(kx, __NV_SATFINITE, __NV_E4M3);
+    *reinterpret_cast<__nv_fp8x2_storage_t*>(vd + i) = __nv_cvt_float2_to_fp8x2(vx, __NV_SATFINITE, __NV_E4M3);
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -138,6 +168,45 @@ extern "C" int kl_paged_kv_append(int dtype, void* k_cache, void* v_cache, const
     kv_append_scalar<float><<<batch, kAppendThreads, 0, st>>>(a);
   } else {
     kv_append_scalar<uint16_t><<<batch, kAppendThreads, 0, st>>>(a);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int kl_paged_kv_append_fp8(int dtype, void* k_cache, void* v_cache, const void* k_new, const void* v_new,
+                                      const float* k_scale, const float* v_scale, const int32_t* block_table,
+                                      const int32_t* positions, int batch, int num_kv_heads, int head_dim,
+                                      int page_size, int64_t block_table_stride, int max_pages_per_seq,
+                                      int64_t num_pages, int64_t new_row_stride, uint32_t* status, void* stream) {
+  using namespace klb;
+  if (batch == 0) return 0;
+  if (batch < 0 || num_kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0 || page_size <= 0 ||
+      max_pages_per_seq < 0 || block_table_stride < max_pages_per_seq || !k_cache || !v_cache || !k_new || !v_new ||
+      !k_scale || !v_scale || !block_table || !positions) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (dtype != KL_FLOAT32 && dtype != KL_FLOAT16 && dtype != KL_BFLOAT16) return static_cast<int>(cudaErrorInvalidValue);
+  const int64_t row_elems = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (row_elems > (1 << 24) || new_row_stride < row_elems) return static_cast<int>(cudaErrorInvalidValue);
+  AppendArgs a{};
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.block_table = block_table;
+  a.positions = positions;
+  a.bt_stride = block_table_stride;
+  a.new_stride = new_row_stride;
+  a.num_pages = num_pages;
+  a.max_pages = max_pages_per_seq;
+  a.page_size = page_size;
+  a.row_elems = static_cast<int>(row_elems);
+  a.elem_bytes = 1;
+  a.status = status;
+  const auto st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case KL_FLOAT32: kv_append_e4m3<float><<<batch, kAppendThreads, 0, st>>>(a, k_scale, v_scale, head_dim); break;
+    case KL_FLOAT16: kv_append_e4m3<__half><<<batch, kAppendThreads, 0, st>>>(a, k_scale, v_scale, head_dim); break;
+    default: kv_append_e4m3<__nv_bfloat16><<<batch, kAppendThreads, 0, st>>>(a, k_scale, v_scale, head_dim); break;
   }
   return static_cast<int>(cudaGetLastError());
 }

@@ -54,6 +54,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernel_lab_b200.h"
@@ -91,6 +92,8 @@ struct DecodeArgs {
   uint32_t* sync;       // [0] status, [1 + (b*Hkv + kvh)*kMaxHeadGroups + hg] arrival counters
   float* part_o;        // [slot][slot_heads][head_dim]
   float* part_lse;      // [slot][slot_heads]
+  const float* k_scale;  // e4m3 cache: per-KV-head dequantisation scales (null otherwise)
+  const float* v_scale;
 };
 
 struct TcShape {
@@ -427,9 +430,9 @@ struct TcLayout {
 
 __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int nstage, int batch) {
+__host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int nstage, int batch, int eb = 2) {
   TcLayout L{};
-  L.head_bytes = kTile * D * 2u;  // one head's K (or V) rows of a tile: D/64 swizzled 2 KB chunks
+  L.head_bytes = kTile * D * eb;  // one head's K (or V) rows of a tile (eb bytes per element)
   L.half = HT * L.head_bytes;
   L.stage_bytes = 2u * L.half;
   uint32_t off = 0;
@@ -455,18 +458,23 @@ __host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int
   return L;
 }
 
-template <typename T, int D, int NT>
+template <typename T, int D, int NT, bool KV8>
 __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                                   const __grid_constant__ CUtensorMap tmv,
                                                                   const DecodeArgs a, const TcShape cfg) {
-  constexpr int NCH = D / 64;  // 128-byte pieces of one head's row of K (or V)
-  constexpr int KS = D / 16;   // k-steps of K.Q^T, and m-tiles of V^T.P^T
-  constexpr int HPW = 8 * NT;  // query heads per consumer warp
+  // KV8: the cache holds e4m3 (one byte per element, per-KV-head scales) and the MMAs run in
+  // f16 (e4m3 converts to f16 exactly); otherwise the cache and the MMAs use T.
+  using MT = typename std::conditional<KV8, __half, T>::type;
+  constexpr int EB = KV8 ? 1 : 2;     // cache bytes per element
+  constexpr int NCH = D * EB / 128;   // 128-byte pieces of one head's row of K (or V)
+  constexpr int KS = D / 16;          // k-steps of K.Q^T, and m-tiles of V^T.P^T
+  constexpr int HPW = 8 * NT;         // query heads per consumer warp
+  constexpr int OW = 128 / (8 * EB);  // consecutive output values a lane owns per piece (8 or 16)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int HT = cfg.ht, HG = cfg.hg, TW = cfg.tw, nstage = cfg.nstage;
-  const TcLayout L = tc_layout(D, NT, HT, TW, nstage, a.batch);
+  const TcLayout L = tc_layout(D, NT, HT, TW, nstage, a.batch, EB);
   const uint32_t ring = smem_u32(smem + L.ring);
   const uint32_t bars = smem_u32(smem + L.bars);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m);
@@ -646,7 +654,8 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     uint32_t published = 0;
     if (!s.whole && tw == 0 && lane == 0) published = ld_relaxed_gpu(counter_of(a, s.b, kvh, hg));
 
-    // Q^T as the B operand, in the permuted contraction order: one 16-byte load per 32 d.
+    // Q^T as the B operand, in the permuted contraction order of the K loads: one 16-byte load
+    // per 32 d (16-bit cache) or two per 64 d (e4m3 cache, converted to f16).
     uint32_t qf[KS][NT][2];
     const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
 #pragma unroll
@@ -654,15 +663,32 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       const int h = hg * HPW + nt * 8 + g;
       const bool hv = h < G;
       const uint4* qrow = reinterpret_cast<const uint4*>(qb + static_cast<int64_t>(hv ? h : 0) * D);
+      if constexpr (!KV8) {
 #pragma unroll
-      for (int kk = 0; kk < D / 32; ++kk) {
-        const uint4 v = hv ? __ldg(qrow + kk * 4 + t4) : make_uint4(0u, 0u, 0u, 0u);
-        qf[2 * kk][nt][0] = v.x;
-        qf[2 * kk][nt][1] = v.y;
-        qf[2 * kk + 1][nt][0] = v.z;
-        qf[2 * kk + 1][nt][1] = v.w;
+        for (int kk = 0; kk < D / 32; ++kk) {
+          const uint4 v = hv ? __ldg(qrow + kk * 4 + t4) : make_uint4(0u, 0u, 0u, 0u);
+          qf[2 * kk][nt][0] = v.x;
+          qf[2 * kk][nt][1] = v.y;
+          qf[2 * kk + 1][nt][0] = v.z;
+          qf[2 * kk + 1][nt][1] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < D / 64; ++kk) {  // d = 64kk + 16t4 + 0..15 feed k-steps 4kk..4kk+3
+          const uint4 v0 = hv ? __ldg(qrow + kk * 8 + 2 * t4) : make_uint4(0u, 0u, 0u, 0u);
+          const uint4 v1 = hv ? __ldg(qrow + kk * 8 + 2 * t4 + 1) : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t wq[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            qf[4 * kk + jj][nt][0] = to_f16x2<T>(wq[2 * jj]);
+            qf[4 * kk + jj][nt][1] = to_f16x2<T>(wq[2 * jj + 1]);
+          }
+        }
       }
     }
+    // e4m3 cache: the K scale folds into the softmax multiplier, the V scale into the output.
+    const float sl_h = KV8 ? sl * __ldg(a.k_scale + kvh) : sl;
+    const float v_scale = KV8 ? __ldg(a.v_scale + kvh) : 1.0f;
 
     float m_run[NT][2], l_run[NT][2], acc[KS][NT][4];
 #pragma unroll
@@ -698,11 +724,24 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           const int u = par * 4 + t4;
           const uint4 x = lds128(sk + ra * 128 + ((u ^ (ra & 7)) << 4));
           const uint4 y = lds128(sk + rb * 128 + ((u ^ (rb & 7)) << 4));
-          const int j0 = 4 * c + 2 * par;
+          if constexpr (!KV8) {
+            const int j0 = 4 * c + 2 * par;
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            Mma<T>::run(sc[nt], x.x, y.x, x.y, y.y, qf[j0][nt][0], qf[j0][nt][1]);
-            Mma<T>::run(sc[nt], x.z, y.z, x.w, y.w, qf[j0 + 1][nt][0], qf[j0 + 1][nt][1]);
+            for (int nt = 0; nt < NT; ++nt) {
+              Mma<MT>::run(sc[nt], x.x, y.x, x.y, y.y, qf[j0][nt][0], qf[j0][nt][1]);
+              Mma<MT>::run(sc[nt], x.z, y.z, x.w, y.w, qf[j0 + 1][nt][0], qf[j0 + 1][nt][1]);
+            }
+          } else {
+            // 16 e4m3 of d = 128c + 64par + 16t4 + 4jj + {0,1 | 2,3} feed k-step 8c + 4par + jj.
+            const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const uint32_t a0 = e4m3x2_to_f16x2(xw[jj]), a2 = e4m3x2_to_f16x2(xw[jj] >> 16);
+              const uint32_t a1 = e4m3x2_to_f16x2(yw[jj]), a3 = e4m3x2_to_f16x2(yw[jj] >> 16);
+              const int j = 8 * c + 4 * par + jj;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(sc[nt], a0, a1, a2, a3, qf[j][nt][0], qf[j][nt][1]);
+            }
           }
         }
       }
@@ -713,7 +752,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[nt][e] *= sl;
+        for (int e = 0; e < 4; ++e) sc[nt][e] *= sl_h;
         if (!row0) sc[nt][0] = sc[nt][1] = -INFINITY;
         if (!row1) sc[nt][2] = sc[nt][3] = -INFINITY;
         float alpha[2];
@@ -728,11 +767,11 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           m_run[nt][e] = mn;
         }
         const uint32_t p01 =
-            Storage<T>::pack2(fast_exp2(sc[nt][0] - m_run[nt][0]), fast_exp2(sc[nt][1] - m_run[nt][1]));
+            Storage<MT>::pack2(fast_exp2(sc[nt][0] - m_run[nt][0]), fast_exp2(sc[nt][1] - m_run[nt][1]));
         const uint32_t p23 =
-            Storage<T>::pack2(fast_exp2(sc[nt][2] - m_run[nt][0]), fast_exp2(sc[nt][3] - m_run[nt][1]));
+            Storage<MT>::pack2(fast_exp2(sc[nt][2] - m_run[nt][0]), fast_exp2(sc[nt][3] - m_run[nt][1]));
         // The normaliser sums the rounded probabilities the MMA actually uses.
-        const float2 f01 = Storage<T>::unpack2(p01), f23 = Storage<T>::unpack2(p23);
+        const float2 f01 = Storage<MT>::unpack2(p01), f23 = Storage<MT>::unpack2(p23);
         l_run[nt][0] = l_run[nt][0] * alpha[0] + (f01.x + f23.x);
         l_run[nt][1] = l_run[nt][1] * alpha[1] + (f01.y + f23.y);
 #pragma unroll
@@ -763,13 +802,27 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         const uint32_t vc[4] = {v[2].x, v[2].y, v[2].z, v[2].w};
         const uint32_t vd[4] = {v[3].x, v[3].y, v[3].z, v[3].w};
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          const uint32_t a0 = __byte_perm(va[mt], vb[mt], 0x5410);
-          const uint32_t a1 = __byte_perm(va[mt], vb[mt], 0x7632);
-          const uint32_t a2 = __byte_perm(vc[mt], vd[mt], 0x5410);
-          const uint32_t a3 = __byte_perm(vc[mt], vd[mt], 0x7632);
+        for (int mt = 0; mt < OW / 2; ++mt) {
+          // m-tile c*OW/2 + mt: row g holds d = 8*OW*c + OW*g + 2mt (the lane's output value 2mt
+          // of piece c), row g + 8 holds d + 1; columns are tokens 2t4, 2t4+1, 2t4+8, 2t4+9.
+          uint32_t w0, w1, w2, w3;
+          if constexpr (!KV8) {
+            w0 = va[mt], w1 = vb[mt], w2 = vc[mt], w3 = vd[mt];
+          } else {
+            const int sh = (mt & 1) * 16;
+            w0 = e4m3x2_to_f16x2(va[mt >> 1] >> sh);
+            w1 = e4m3x2_to_f16x2(vb[mt >> 1] >> sh);
+            w2 = e4m3x2_to_f16x2(vc[mt >> 1] >> sh);
+            w3 = e4m3x2_to_f16x2(vd[mt >> 1] >> sh);
+          }
+          const uint32_t a0 = __byte_perm(w0, w1, 0x5410);
+          const uint32_t a1 = __byte_perm(w0, w1, 0x7632);
+          const uint32_t a2 = __byte_perm(w2, w3, 0x5410);
+          const uint32_t a3 = __byte_perm(w2, w3, 0x7632);
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(acc[c * 4 + mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          for (int nt = 0; nt < NT; ++nt) {
+            Mma<MT>::run(acc[c * (OW / 2) + mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+          }
         }
       }
       __syncwarp();
@@ -790,8 +843,8 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       }
     }
 
-    // Lane (g, t4) owns, for head hl = nt*8 + 2*t4 + e and piece c, output d = 64c + 8g + k,
-    // k = 0..7, held in acc[4c + k/2][nt][e + 2*(k & 1)].
+    // Lane (g, t4) owns, for head hl = nt*8 + 2*t4 + e and piece c, output d = 8*OW*c + OW*g + k,
+    // k = 0..OW-1, held in acc[c*OW/2 + k/2][nt][e + 2*(k & 1)].
     // Warps that split the tiles of one (head, group) combine into the tw == 0 warp.
     if (TW > 1) {
       if (tw != 0) {
@@ -810,9 +863,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
             }
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
-              float* dst = ra + hl * (D + 4) + c * 64 + 8 * g;
+              float* dst = ra + hl * (D + 4) + c * 8 * OW + OW * g;
 #pragma unroll
-              for (int k = 0; k < 8; ++k) dst[k] = acc[c * 4 + (k >> 1)][nt][e + 2 * (k & 1)];
+              for (int k = 0; k < OW; ++k) dst[k] = acc[c * (OW / 2) + (k >> 1)][nt][e + 2 * (k & 1)];
             }
           }
         }
@@ -844,7 +897,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
               for (int c = 0; c < NCH; ++c) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) acc[c * 4 + (k >> 1)][nt][e + 2 * (k & 1)] += src[c * 64 + 8 * g + k] * f;
+                for (int k = 0; k < OW; ++k) {
+                  acc[c * (OW / 2) + (k >> 1)][nt][e + 2 * (k & 1)] += src[c * 8 * OW + OW * g + k] * f;
+                }
               }
             }
             m_run[nt][e] = M;
@@ -866,16 +921,20 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         for (int e = 0; e < 2; ++e) {
           const int hl = nt * 8 + 2 * t4 + e;
           if (hg * HPW + hl >= G) continue;
-          const float inv = l_run[nt][e] > 0.0f ? 1.0f / l_run[nt][e] : 0.0f;
+          const float inv = l_run[nt][e] > 0.0f ? v_scale / l_run[nt][e] : 0.0f;
           T* orow = out + (out_row0 + hl) * D;
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {
-            uint4 pk;
-            pk.x = Storage<T>::pack2(acc[c * 4 + 0][nt][e] * inv, acc[c * 4 + 0][nt][e + 2] * inv);
-            pk.y = Storage<T>::pack2(acc[c * 4 + 1][nt][e] * inv, acc[c * 4 + 1][nt][e + 2] * inv);
-            pk.z = Storage<T>::pack2(acc[c * 4 + 2][nt][e] * inv, acc[c * 4 + 2][nt][e + 2] * inv);
-            pk.w = Storage<T>::pack2(acc[c * 4 + 3][nt][e] * inv, acc[c * 4 + 3][nt][e + 2] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 64 + 8 * g) = pk;
+#pragma unroll
+            for (int h = 0; h < OW / 8; ++h) {
+              const int m0 = c * (OW / 2) + 4 * h;
+              uint4 pk;
+              pk.x = Storage<T>::pack2(acc[m0 + 0][nt][e] * inv, acc[m0 + 0][nt][e + 2] * inv);
+              pk.y = Storage<T>::pack2(acc[m0 + 1][nt][e] * inv, acc[m0 + 1][nt][e + 2] * inv);
+              pk.z = Storage<T>::pack2(acc[m0 + 2][nt][e] * inv, acc[m0 + 2][nt][e + 2] * inv);
+              pk.w = Storage<T>::pack2(acc[m0 + 3][nt][e] * inv, acc[m0 + 3][nt][e + 2] * inv);
+              *reinterpret_cast<uint4*>(orow + c * 8 * OW + OW * g + 8 * h) = pk;
+            }
           }
         }
       }
@@ -889,7 +948,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float l = l_run[nt][e];
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        const float inv = l > 0.0f ? v_scale / l : 0.0f;
         lse_own[nt][e] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
@@ -915,11 +974,12 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           float* po = a.part_o + (slot * HPW + hl) * D;
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {
-            float4* dst = reinterpret_cast<float4*>(po + c * 64 + 8 * g);
-            dst[0] = make_float4(acc[c * 4 + 0][nt][e], acc[c * 4 + 0][nt][e + 2], acc[c * 4 + 1][nt][e],
-                                 acc[c * 4 + 1][nt][e + 2]);
-            dst[1] = make_float4(acc[c * 4 + 2][nt][e], acc[c * 4 + 2][nt][e + 2], acc[c * 4 + 3][nt][e],
-                                 acc[c * 4 + 3][nt][e + 2]);
+            float4* dst = reinterpret_cast<float4*>(po + c * 8 * OW + OW * g);
+#pragma unroll
+            for (int h = 0; h < OW / 4; ++h) {
+              const int m0 = c * (OW / 2) + 2 * h;
+              dst[h] = make_float4(acc[m0][nt][e], acc[m0][nt][e + 2], acc[m0 + 1][nt][e], acc[m0 + 1][nt][e + 2]);
+            }
           }
           if (g == 0) a.part_lse[slot * HPW + hl] = lse_own[nt][e];
         }
@@ -961,7 +1021,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         for (int ne = 0; ne < NT * 2; ne += EG) {
           const int nt = ne / 2;
           float lse[EG];
-          float4 x[EG][NCH][2];
+          float4 x[EG][NCH][OW / 4];
 #pragma unroll
           for (int ei = 0; ei < EG; ++ei) {
             const int e = ne % 2 + ei;
@@ -972,11 +1032,11 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float* lo = &acc[c * 4 + 2 * h][nt][0];
-                const float* hi = &acc[c * 4 + 2 * h + 1][nt][0];
+              for (int h = 0; h < OW / 4; ++h) {
+                const float* lo = &acc[c * (OW / 2) + 2 * h][nt][0];
+                const float* hi = &acc[c * (OW / 2) + 2 * h + 1][nt][0];
                 x[ei][c][h] = own ? make_float4(lo[e], lo[e + 2], hi[e], hi[e + 2])
-                            : ld  ? __ldcg(reinterpret_cast<const float4*>(po + c * 64 + 8 * g + 4 * h))
+                            : ld  ? __ldcg(reinterpret_cast<const float4*>(po + c * 8 * OW + OW * g + 4 * h))
                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
               }
             }
@@ -992,9 +1052,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                float* lo = &o_acc[c * 4 + 2 * h][nt][0];
-                float* hi = &o_acc[c * 4 + 2 * h + 1][nt][0];
+              for (int h = 0; h < OW / 4; ++h) {
+                float* lo = &o_acc[c * (OW / 2) + 2 * h][nt][0];
+                float* hi = &o_acc[c * (OW / 2) + 2 * h + 1][nt][0];
                 lo[e] = lo[e] * fa + fb * x[ei][c][h].x;
                 lo[e + 2] = lo[e + 2] * fa + fb * x[ei][c][h].y;
                 hi[e] = hi[e] * fa + fb * x[ei][c][h].z;
@@ -1014,12 +1074,16 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           T* orow = out + (out_row0 + hl) * D;
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {
-            uint4 pk;
-            pk.x = Storage<T>::pack2(o_acc[c * 4 + 0][nt][e] * inv, o_acc[c * 4 + 0][nt][e + 2] * inv);
-            pk.y = Storage<T>::pack2(o_acc[c * 4 + 1][nt][e] * inv, o_acc[c * 4 + 1][nt][e + 2] * inv);
-            pk.z = Storage<T>::pack2(o_acc[c * 4 + 2][nt][e] * inv, o_acc[c * 4 + 2][nt][e + 2] * inv);
-            pk.w = Storage<T>::pack2(o_acc[c * 4 + 3][nt][e] * inv, o_acc[c * 4 + 3][nt][e + 2] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 64 + 8 * g) = pk;
+#pragma unroll
+            for (int h = 0; h < OW / 8; ++h) {
+              const int m0 = c * (OW / 2) + 4 * h;
+              uint4 pk;
+              pk.x = Storage<T>::pack2(o_acc[m0 + 0][nt][e] * inv, o_acc[m0 + 0][nt][e + 2] * inv);
+              pk.y = Storage<T>::pack2(o_acc[m0 + 1][nt][e] * inv, o_acc[m0 + 1][nt][e + 2] * inv);
+              pk.z = Storage<T>::pack2(o_acc[m0 + 2][nt][e] * inv, o_acc[m0 + 2][nt][e + 2] * inv);
+              pk.w = Storage<T>::pack2(o_acc[m0 + 3][nt][e] * inv, o_acc[m0 + 3][nt][e + 2] * inv);
+              *reinterpret_cast<uint4*>(orow + c * 8 * OW + OW * g + 8 * h) = pk;
+            }
           }
         }
       }
@@ -1232,6 +1296,7 @@ struct Plan {
   int slots = 0, slot_heads = 0;
   int seg_cost = 0;
   int min_tiles = kMinTilesPerCta;
+  bool kv8 = false;
   size_t part_bytes = 0, sync_bytes = 0;
   const void* fn = nullptr;
 };
@@ -1272,10 +1337,20 @@ int blocks_per_sm(int dev, const void* fn, int threads, size_t smem) {
 }
 
 template <typename T>
-const void* tc_fn(int D, int NT) {
-  if (D == 64) return NT == 1 ? (const void*)decode_tc_kernel<T, 64, 1> : (const void*)decode_tc_kernel<T, 64, 2>;
-  if (D == 128) return NT == 1 ? (const void*)decode_tc_kernel<T, 128, 1> : (const void*)decode_tc_kernel<T, 128, 2>;
-  return (const void*)decode_tc_kernel<T, 256, 1>;
+const void* tc_fn(int D, int NT, bool kv8) {
+  if (kv8) {
+    if (D == 128) {
+      return NT == 1 ? (const void*)decode_tc_kernel<T, 128, 1, true> : (const void*)decode_tc_kernel<T, 128, 2, true>;
+    }
+    return (const void*)decode_tc_kernel<T, 256, 1, true>;
+  }
+  if (D == 64) {
+    return NT == 1 ? (const void*)decode_tc_kernel<T, 64, 1, false> : (const void*)decode_tc_kernel<T, 64, 2, false>;
+  }
+  if (D == 128) {
+    return NT == 1 ? (const void*)decode_tc_kernel<T, 128, 1, false> : (const void*)decode_tc_kernel<T, 128, 2, false>;
+  }
+  return (const void*)decode_tc_kernel<T, 256, 1, false>;
 }
 
 const void* gen_fn(int dtype) {
@@ -1308,8 +1383,9 @@ size_t lse_offset(int slots, int slot_heads, int D) {
 }
 
 // Launch shape and scratch sizes of one decode call. `generic` forces the CUDA-core kernel.
+// kv8: e4m3 cache (tensor-core kernel only: head_dim 128 or 256, q/out fp16 or bf16).
 int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages, int num_splits, bool generic,
-              Plan& p) {
+              Plan& p, bool kv8 = false) {
   if (batch <= 0 || batch > kMaxBatch || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || D <= 0 || P <= 0 ||
       max_pages < 0 || num_splits < 0) {
     return static_cast<int>(cudaErrorInvalidValue);
@@ -1329,8 +1405,11 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   const int NT = (G > 8 && D <= 128) ? 2 : 1;
   const int hg_need = (G + 8 * NT - 1) / (8 * NT);
   const int HG = hg_need <= 1 ? 1 : hg_need <= 2 ? 2 : hg_need <= 4 ? 4 : 0;
-  p.tc = !generic && dtype != KL_FLOAT32 && (D == 64 || D == 128 || D == 256) && (P == 8 || P % 16 == 0) &&
-         HG > 0;
+  p.tc = !generic && dtype != KL_FLOAT32 && (D == (kv8 ? 128 : 64) || D == 128 || D == 256) &&
+         (P == 8 || P % 16 == 0) && HG > 0;
+  if (kv8 && !p.tc) return static_cast<int>(cudaErrorInvalidValue);
+  p.kv8 = kv8;
+  const int eb = kv8 ? 1 : 2;
   int threads;
   if (p.tc) {
     p.NT = NT;
@@ -1348,7 +1427,7 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     p.shape.hg = HG;
     p.shape.tw = kCW / (ht * HG);
     p.shape.p_rows = P < 16 ? P : 16;
-    const TcLayout base = tc_layout(D, NT, ht, p.shape.tw, 0, batch);
+    const TcLayout base = tc_layout(D, NT, ht, p.shape.tw, 0, batch, eb);
     const uint32_t stage = base.stage_bytes + 16u;
     int ns = base.total < kTcSmemBudget ? static_cast<int>((kTcSmemBudget - base.total) / stage) : 0;
     ns = std::min(kMaxStages, ns);
@@ -1361,8 +1440,8 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     ns = ns / p.shape.tw * p.shape.tw;
     if (ns < std::max(2, p.shape.tw)) return static_cast<int>(cudaErrorInvalidValue);
     p.shape.nstage = ns;
-    p.smem = tc_layout(D, NT, ht, p.shape.tw, ns, batch).total;
-    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, NT) : tc_fn<__nv_bfloat16>(D, NT);
+    p.smem = tc_layout(D, NT, ht, p.shape.tw, ns, batch, eb).total;
+    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, NT, kv8) : tc_fn<__nv_bfloat16>(D, NT, kv8);
     p.units = Hkv / ht;
     p.slot_heads = 8 * NT;
     threads = kTCThreads;
@@ -1428,15 +1507,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 // p_rows tokens is one tile (or half of one, for page size 8) of a head block: for HT == Hkv a
 // whole page, read front to back.
 bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_tokens, int Hkv, int D, int HT,
-                   int p_rows) {
+                   int p_rows, bool kv8) {
   auto enc = encoder();
   if (!enc) return false;
-  const cuuint64_t dims[3] = {64u, static_cast<cuuint64_t>(Hkv) * D / 64, static_cast<cuuint64_t>(pool_tokens)};
-  const cuuint64_t strides[2] = {128u, static_cast<cuuint64_t>(Hkv) * D * 2};
-  const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(HT * D / 64), static_cast<cuuint32_t>(p_rows)};
+  // 128-byte pieces: 64 two-byte elements, or 128 e4m3 bytes (moved as uint8).
+  const int per_piece = kv8 ? 128 : 64;
+  const int row_bytes = Hkv * D * (kv8 ? 1 : 2);
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(per_piece), static_cast<cuuint64_t>(row_bytes / 128),
+                              static_cast<cuuint64_t>(pool_tokens)};
+  const cuuint64_t strides[2] = {128u, static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(per_piece), static_cast<cuuint32_t>(HT * D * (kv8 ? 1 : 2) / 128),
+                             static_cast<cuuint32_t>(p_rows)};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUtensorMapDataType dt =
-      dtype == KL_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType dt = kv8                  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : dtype == KL_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1445,36 +1530,46 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_t
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-template <typename T>
-cudaError_t launch_tc(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                      cudaStream_t st) {
-  switch (p.D) {
-    case 64:
-      if (p.NT == 1) decode_tc_kernel<T, 64, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      else decode_tc_kernel<T, 64, 2><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      break;
-    case 128:
-      if (p.NT == 1) decode_tc_kernel<T, 128, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      else decode_tc_kernel<T, 128, 2><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      break;
-    default:
-      decode_tc_kernel<T, 256, 1><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      break;
+template <typename T, bool KV8>
+cudaError_t launch_tc_kind(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                           cudaStream_t st) {
+  if constexpr (!KV8) {
+    if (p.D == 64) {
+      if (p.NT == 1) decode_tc_kernel<T, 64, 1, false><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+      else decode_tc_kernel<T, 64, 2, false><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+      return cudaGetLastError();
+    }
+  }
+  if (p.D == 128) {
+    if (p.NT == 1) decode_tc_kernel<T, 128, 1, KV8><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+    else decode_tc_kernel<T, 128, 2, KV8><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+  } else {
+    decode_tc_kernel<T, 256, 1, KV8><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
   }
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t launch_tc(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                      cudaStream_t st) {
+  return p.kv8 ? launch_tc_kind<T, true>(p, tmk, tmv, a, st) : launch_tc_kind<T, false>(p, tmk, tmv, a, st);
+}
+
+// k_scale / v_scale non-null: the caches hold e4m3 (tensor-core kernel only, no fallback).
 int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
                 const int32_t* block_table, const int32_t* seq_lens, int batch, int Hq, int Hkv, int D, int P,
                 int64_t bt_stride, int max_pages, int64_t num_pages, float scale, int num_splits, void* partials,
-                size_t partial_bytes, void* sync, size_t sync_bytes, cudaStream_t st) {
+                size_t partial_bytes, void* sync, size_t sync_bytes, cudaStream_t st,
+                const float* k_scale = nullptr, const float* v_scale = nullptr) {
   if (batch == 0) return 0;
   if (!out || !q || !k_cache || !v_cache || !block_table || !seq_lens || !sync) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
+  const bool kv8 = k_scale != nullptr || v_scale != nullptr;
+  if (kv8 && (!k_scale || !v_scale)) return static_cast<int>(cudaErrorInvalidValue);
   if (bt_stride < 0 || (batch > 1 && bt_stride < max_pages)) return static_cast<int>(cudaErrorInvalidValue);
   Plan p;
-  if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p)) return rc;
+  if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p, kv8)) return rc;
   // The tensor-core path needs 16-byte aligned caches (TMA), q and out (vector loads and
   // stores) and TMA row coordinates that fit in int32; otherwise take the generic kernel.
   const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 16) && aligned(out, 16) &&
@@ -1483,9 +1578,10 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   bool use_tc = false;
   if (tc_ok) {
     const int64_t pool_tokens = num_pages >= 0 ? std::max<int64_t>(num_pages, 1) * P : (int64_t(1) << 31) - 1;
-    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows) &&
-             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows);
+    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8) &&
+             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8);
   }
+  if (kv8 && !use_tc) return static_cast<int>(cudaErrorInvalidValue);  // no generic e4m3 kernel
   if (!use_tc && p.tc) {
     if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, true, p)) return rc;
   }
@@ -1517,6 +1613,8 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   a.sync = static_cast<uint32_t*>(sync);
   a.part_o = static_cast<float*>(partials);
   a.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + lse_offset(p.slots, p.slot_heads, D));
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
 
   if (use_tc) {
     const cudaError_t e = dtype == KL_FLOAT16 ? launch_tc<__half>(p, tmk, tmv, a, st)
@@ -1573,6 +1671,19 @@ int kl_paged_decode(int dtype, void* out, const void* q, const void* k_cache, co
   return klb::decode_impl(dtype, out, q, k_cache, v_cache, block_table, seq_lens, batch, num_q_heads, num_kv_heads,
                           head_dim, page_size, block_table_stride, max_pages_per_seq, num_pages, scale, num_splits,
                           partials, partial_bytes, sync, sync_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int kl_paged_decode_fp8(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                        const float* k_scale, const float* v_scale, const int32_t* block_table,
+                        const int32_t* seq_lens, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                        int page_size, int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
+                        float scale, int num_splits, void* partials, size_t partial_bytes, void* sync,
+                        size_t sync_bytes, void* stream) {
+  if (batch != 0 && (!k_scale || !v_scale)) return static_cast<int>(cudaErrorInvalidValue);
+  return klb::decode_impl(dtype, out, q, k_cache, v_cache, block_table, seq_lens, batch, num_q_heads, num_kv_heads,
+                          head_dim, page_size, block_table_stride, max_pages_per_seq, num_pages, scale, num_splits,
+                          partials, partial_bytes, sync, sync_bytes, static_cast<cudaStream_t>(stream), k_scale,
+                          v_scale);
 }
 
 int kl_paged_decode_attention(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,

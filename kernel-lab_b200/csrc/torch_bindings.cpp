@@ -208,6 +208,107 @@ void paged_kv_append(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor&
                "paged_kv_append");
 }
 
+bool is_e4m3(const at::Tensor& t) { return t.scalar_type() == at::kFloat8_e4m3fn || t.scalar_type() == at::kByte; }
+
+void check_scales(const at::Tensor& k_scale, const at::Tensor& v_scale, int64_t num_kv_heads, const at::Device& dev) {
+  TORCH_CHECK(k_scale.scalar_type() == at::kFloat && v_scale.scalar_type() == at::kFloat &&
+                  k_scale.is_contiguous() && v_scale.is_contiguous() && k_scale.numel() == num_kv_heads &&
+                  v_scale.numel() == num_kv_heads && k_scale.device() == dev && v_scale.device() == dev,
+              "k_scale and v_scale are contiguous float32 [num_kv_heads] on the caches' device");
+}
+
+// Decode over an e4m3 cache with per-KV-head scales (kl_paged_decode_fp8).
+void paged_decode_attention_fp8(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                                const at::Tensor& v_cache, const at::Tensor& k_scale, const at::Tensor& v_scale,
+                                const at::Tensor& block_table, const at::Tensor& seq_lens, double scale) {
+  TORCH_CHECK(q.is_cuda() && k_cache.is_cuda() && v_cache.is_cuda(), "tensors must be on CUDA");
+  TORCH_CHECK(q.dim() == 3 && k_cache.dim() == 4, "q is [batch, heads, dim]; caches are 4-D");
+  TORCH_CHECK(q.is_contiguous() && out.is_contiguous() && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "q, out and both caches must be contiguous");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k_cache and v_cache shapes differ");
+  TORCH_CHECK(is_e4m3(k_cache) && is_e4m3(v_cache), "caches must be float8_e4m3fn (or uint8 e4m3 codes)");
+  TORCH_CHECK((q.scalar_type() == at::kHalf || q.scalar_type() == at::kBFloat16) &&
+                  out.scalar_type() == q.scalar_type() && out.sizes() == q.sizes(),
+              "q and out are fp16 or bf16 of one shape");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  block_table.dim() == 2 && block_table.stride(-1) == 1 && seq_lens.is_contiguous(),
+              "block_table rows and seq_lens must be contiguous int32");
+  TORCH_CHECK(k_cache.device() == q.device() && v_cache.device() == q.device() && out.device() == q.device() &&
+                  block_table.device() == q.device() && seq_lens.device() == q.device(),
+              "tensors must be on one device");
+  const int batch = static_cast<int>(q.size(0));
+  const int num_q_heads = static_cast<int>(q.size(1));
+  const int head_dim = static_cast<int>(q.size(2));
+  const int page_size = static_cast<int>(k_cache.size(1));
+  const int num_kv_heads = static_cast<int>(k_cache.size(2));
+  TORCH_CHECK(k_cache.size(3) == head_dim, "cache head_dim differs from q");
+  TORCH_CHECK(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "num_q_heads must be a multiple of num_kv_heads");
+  TORCH_CHECK(seq_lens.numel() == batch && block_table.size(0) == batch,
+              "block_table and seq_lens need one row / entry per sequence");
+  check_scales(k_scale, v_scale, num_kv_heads, q.device());
+  if (batch == 0) return;
+  const int dtype = to_dtype(q.scalar_type());
+  const int max_pages = static_cast<int>(block_table.size(1));
+  const c10::cuda::CUDAGuard guard(q.device());
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  size_t partial_bytes = 0, sync_bytes = 0;
+  check_status(kl_paged_decode_workspace_size(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size,
+                                              max_pages, 0, &partial_bytes, &sync_bytes),
+               "paged_decode_attention_fp8 (workspace)");
+  Scratch& s = scratch_for(q.device(), stream, partial_bytes, sync_bytes);
+  check_status(kl_paged_decode_fp8(dtype, out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                   k_scale.data_ptr<float>(), v_scale.data_ptr<float>(),
+                                   block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), batch,
+                                   num_q_heads, num_kv_heads, head_dim, page_size, block_table.stride(0), max_pages,
+                                   k_cache.size(0), static_cast<float>(scale), 0, s.partials.data_ptr(),
+                                   static_cast<size_t>(s.partials.numel()), s.sync.data_ptr(),
+                                   static_cast<size_t>(s.sync.numel()), stream),
+               "paged_decode_attention_fp8");
+}
+
+// Quantising append into an e4m3 cache (kl_paged_kv_append_fp8).
+void paged_kv_append_fp8(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor& k_new, const at::Tensor& v_new,
+                         const at::Tensor& k_scale, const at::Tensor& v_scale, const at::Tensor& block_table,
+                         const at::Tensor& positions) {
+  TORCH_CHECK(k_cache.is_cuda() && v_cache.is_cuda() && k_new.is_cuda() && v_new.is_cuda(),
+              "tensors must be on CUDA");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous() &&
+                  k_cache.sizes() == v_cache.sizes() && is_e4m3(k_cache) && is_e4m3(v_cache),
+              "caches are contiguous e4m3 [num_pages, page_size, num_kv_heads, head_dim] of one shape");
+  const int64_t num_kv_heads = k_cache.size(2), head_dim = k_cache.size(3);
+  TORCH_CHECK(k_new.sizes() == v_new.sizes() && k_new.strides() == v_new.strides() &&
+                  k_new.scalar_type() == v_new.scalar_type(),
+              "k_new and v_new must have one shape, layout and dtype");
+  TORCH_CHECK((k_new.dim() == 3 && k_new.size(1) == num_kv_heads && k_new.size(2) == head_dim &&
+               k_new.stride(2) == 1 && k_new.stride(1) == head_dim) ||
+                  (k_new.dim() == 2 && k_new.size(1) == num_kv_heads * head_dim && k_new.stride(1) == 1),
+              "k_new is [batch, num_kv_heads, head_dim] (or [batch, num_kv_heads*head_dim]) with contiguous rows");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && positions.scalar_type() == at::kInt &&
+                  block_table.dim() == 2 && block_table.stride(-1) == 1 && positions.is_contiguous(),
+              "block_table rows and positions must be contiguous int32");
+  const int64_t batch = k_new.size(0);
+  TORCH_CHECK(positions.numel() == batch && block_table.size(0) == batch,
+              "block_table and positions need one row / entry per sequence");
+  TORCH_CHECK(v_cache.device() == k_cache.device() && k_new.device() == k_cache.device() &&
+                  v_new.device() == k_cache.device() && block_table.device() == k_cache.device() &&
+                  positions.device() == k_cache.device(),
+              "tensors must be on one device");
+  check_scales(k_scale, v_scale, num_kv_heads, k_cache.device());
+  if (batch == 0) return;
+  const c10::cuda::CUDAGuard guard(k_new.device());
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  Scratch& s = scratch_for(k_new.device(), stream, 0, 4);
+  check_status(kl_paged_kv_append_fp8(to_dtype(k_new.scalar_type()), k_cache.data_ptr(), v_cache.data_ptr(),
+                                      k_new.data_ptr(), v_new.data_ptr(), k_scale.data_ptr<float>(),
+                                      v_scale.data_ptr<float>(), block_table.data_ptr<int32_t>(),
+                                      positions.data_ptr<int32_t>(), static_cast<int>(batch),
+                                      static_cast<int>(num_kv_heads), static_cast<int>(head_dim),
+                                      static_cast<int>(k_cache.size(1)), block_table.stride(0),
+                                      static_cast<int>(block_table.size(1)), k_cache.size(0), k_new.stride(0),
+                                      static_cast<uint32_t*>(s.sync.data_ptr()), stream),
+               "paged_kv_append_fp8");
+}
+
 // Status bits (KL_STATUS_*) left by decode calls on the current device and stream.
 int64_t decode_status(bool clear) {
   const at::Device dev(at::kCUDA, c10::cuda::current_device());
@@ -232,6 +333,10 @@ void noop_decode_splits(at::Tensor&, const at::Tensor&, const at::Tensor&, const
                         const at::Tensor&, double, int64_t) {}
 void noop_append(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                  const at::Tensor&) {}
+void noop_decode_fp8(at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                     const at::Tensor&, const at::Tensor&, const at::Tensor&, double) {}
+void noop_append_fp8(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                     const at::Tensor&, const at::Tensor&, const at::Tensor&) {}
 
 }  // namespace
 
@@ -247,6 +352,12 @@ TORCH_LIBRARY(kernel_lab, m) {
   m.def(
       "paged_kv_append(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, "
       "Tensor block_table, Tensor positions) -> ()");
+  m.def(
+      "paged_decode_attention_fp8(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor k_scale, "
+      "Tensor v_scale, Tensor block_table, Tensor seq_lens, float scale) -> ()");
+  m.def(
+      "paged_kv_append_fp8(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, Tensor k_scale, "
+      "Tensor v_scale, Tensor block_table, Tensor positions) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(kernel_lab, CUDA, m) {
@@ -255,6 +366,8 @@ TORCH_LIBRARY_IMPL(kernel_lab, CUDA, m) {
   m.impl("paged_decode_attention", &paged_decode_attention);
   m.impl("paged_decode_attention_splits", &paged_decode_attention_splits);
   m.impl("paged_kv_append", &paged_kv_append);
+  m.impl("paged_decode_attention_fp8", &paged_decode_attention_fp8);
+  m.impl("paged_kv_append_fp8", &paged_kv_append_fp8);
 }
 
 TORCH_LIBRARY_IMPL(kernel_lab, Meta, m) {
@@ -263,6 +376,8 @@ TORCH_LIBRARY_IMPL(kernel_lab, Meta, m) {
   m.impl("paged_decode_attention", &noop_decode);
   m.impl("paged_decode_attention_splits", &noop_decode_splits);
   m.impl("paged_kv_append", &noop_append);
+  m.impl("paged_decode_attention_fp8", &noop_decode_fp8);
+  m.impl("paged_kv_append_fp8", &noop_append_fp8);
 }
 
 // Importing kernel_lab._C runs the registrations above.

@@ -49,6 +49,16 @@ SIGNATURES = {
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int, _c_i64,
          _c_i64, _c_vp, _c_vp],
     ),
+    "kl_paged_decode_fp8": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+         _c_i64, _c_int, _c_i64, _c_float, _c_int, _c_vp, _c_sz, _c_vp, _c_sz, _c_vp],
+    ),
+    "kl_paged_kv_append_fp8": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_i64,
+         _c_int, _c_i64, _c_i64, _c_vp, _c_vp],
+    ),
     "kl_paged_decode_noalloc": (
         _c_int,
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int,
@@ -235,4 +245,61 @@ def paged_kv_append(
             k_new.stride(0), _ptr(status), _stream(stream),
         ),
         "kl_paged_kv_append",
+    )
+
+
+def paged_decode_fp8(
+    out: torch.Tensor,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    k_scale: torch.Tensor,
+    v_scale: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    num_splits: int = 0,
+    scratch: DecodeScratch | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> DecodeScratch:
+    """kl_paged_decode_fp8 on torch tensors (caches of torch.float8_e4m3fn or uint8 codes)."""
+    batch, hq, d = q.shape
+    num_pages, page, hkv, _ = k_cache.shape
+    if scratch is None:
+        scratch = DecodeScratch.for_problem(q, k_cache, block_table, num_splits)
+    scale = d**-0.5 if scale is None else scale
+    _check(
+        load().kl_paged_decode_fp8(
+            DTYPE_CODES[q.dtype], _ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k_scale), _ptr(v_scale),
+            _ptr(block_table), _ptr(seq_lens), batch, hq, hkv, d, page, block_table.stride(0), block_table.shape[1],
+            num_pages, scale, num_splits, _ptr(scratch.partials), scratch.partials.numel(), _ptr(scratch.sync),
+            scratch.sync.numel(), _stream(stream),
+        ),
+        "kl_paged_decode_fp8",
+    )
+    return scratch
+
+
+def paged_kv_append_fp8(
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    k_scale: torch.Tensor,
+    v_scale: torch.Tensor,
+    block_table: torch.Tensor,
+    positions: torch.Tensor,
+    status: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """kl_paged_kv_append_fp8 on torch tensors."""
+    batch = k_new.shape[0]
+    num_pages, page, hkv, d = k_cache.shape
+    _check(
+        load().kl_paged_kv_append_fp8(
+            DTYPE_CODES[k_new.dtype], _ptr(k_cache), _ptr(v_cache), _ptr(k_new), _ptr(v_new), _ptr(k_scale),
+            _ptr(v_scale), _ptr(block_table), _ptr(positions), batch, hkv, d, page, block_table.stride(0),
+            block_table.shape[1], num_pages, k_new.stride(0), _ptr(status), _stream(stream),
+        ),
+        "kl_paged_kv_append_fp8",
     )

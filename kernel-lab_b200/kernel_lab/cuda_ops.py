@@ -92,6 +92,43 @@ def paged_kv_append(
     torch.ops.kernel_lab.paged_kv_append(k_cache, v_cache, k_new, v_new, block_table, positions)
 
 
+def paged_decode_attention_fp8(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    k_scale: torch.Tensor,
+    v_scale: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Decode attention over an e4m3 KV cache (torch.float8_e4m3fn) with per-KV-head float32
+    scales: K = code * k_scale[h], V = code * v_scale[h]. q is fp16 or bf16."""
+    _require()
+    scale = q.shape[-1] ** -0.5 if scale is None else scale
+    out = torch.empty_like(q)
+    torch.ops.kernel_lab.paged_decode_attention_fp8(
+        out, q.contiguous(), k_cache, v_cache, k_scale, v_scale, block_table, seq_lens, scale
+    )
+    return out
+
+
+def paged_kv_append_fp8(
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    k_scale: torch.Tensor,
+    v_scale: torch.Tensor,
+    block_table: torch.Tensor,
+    positions: torch.Tensor,
+) -> None:
+    """paged_kv_append into an e4m3 cache: rows are quantised per KV head as
+    e4m3(x / scale) (round to nearest-even, saturating to +-448)."""
+    _require()
+    torch.ops.kernel_lab.paged_kv_append_fp8(k_cache, v_cache, k_new, v_new, k_scale, v_scale, block_table, positions)
+
+
 def decode_status(clear: bool = False) -> int:
     """KL_STATUS_* bits left by decode and append calls on the current device and stream
     (synchronises)."""

@@ -198,3 +198,18 @@ def random_paged_pool(
             v_cache[page, tail:] = 0
     seq = torch.tensor(lens, dtype=torch.int32, device=dev)
     return q, PagedKV(k_cache=k_cache, v_cache=v_cache, block_table=table, seq_lens=seq, page_size=page_size)
+
+
+def quantize_e4m3(cache: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """A [num_pages, page, num_kv_heads, head_dim] cache as e4m3 codes with per-KV-head scales:
+    e4m3(x / scale[h]), rounded to nearest-even and saturated to +-448 (NaN poison stays NaN),
+    the rounding of the kernels' quantising append."""
+    x = cache.float() / scale.float().view(1, 1, -1, 1)
+    return torch.where(torch.isnan(x), x, x.clamp(-448.0, 448.0)).to(torch.float8_e4m3fn)
+
+
+def e4m3_scales(cache: torch.Tensor, margin: float = 1.0) -> torch.Tensor:
+    """Per-KV-head scales that map each head's largest finite magnitude to 448 / margin."""
+    x = cache.float()
+    amax = torch.where(torch.isfinite(x), x.abs(), torch.zeros_like(x)).amax(dim=(0, 1, 3))
+    return (amax.clamp_min(1e-12) * margin / 448.0).float().contiguous()

@@ -124,6 +124,89 @@ def paged_decode_attention(
 
 KL_STATUS_BAD_PAGE = 1
 
+# ---------------------------------------------------------------- e4m3 (float8 "fn": no infinities)
+#
+# The FP8 KV cache of kernel-lab's roadmap (README.md:98) stores K and V as e4m3 with one
+# scale per KV head: stored = e4m3(x / scale), read = e4m3 value * scale. e4m3: 1 sign bit,
+# 4 exponent bits (bias 7), 3 mantissa bits; subnormals below 2**-6; S.1111.111 is NaN;
+# largest finite 448. Encoding rounds to nearest-even and saturates to +-448 (the cast that
+# the CUDA fp8 conversion performs with its saturate-finite mode). These are restatements
+# of the format's published definition; tests pin them against torch.float8_e4m3fn.
+
+
+def _e4m3_table() -> np.ndarray:
+    b = np.arange(256, dtype=np.int64)
+    sign = np.where(b >> 7, -1.0, 1.0)
+    e = (b >> 3) & 15
+    m = (b & 7).astype(np.float64)
+    mag = np.where(e == 0, m / 8.0 * 2.0**-6, (1.0 + m / 8.0) * 2.0 ** (e - 7))
+    val = sign * mag
+    val[(e == 15) & ((b & 7) == 7)] = np.nan
+    return val.astype(np.float32)
+
+
+E4M3_VALUES = _e4m3_table()
+
+
+def e4m3_decode(bytes_: np.ndarray) -> np.ndarray:
+    """uint8 e4m3 codes -> float32 values."""
+    return E4M3_VALUES[np.asarray(bytes_, dtype=np.uint8)]
+
+
+def e4m3_encode(x: np.ndarray) -> np.ndarray:
+    """float32 -> uint8 e4m3 codes: round to nearest-even, saturate to +-448, NaN stays NaN."""
+    x = np.asarray(x, dtype=np.float32)
+    a = np.where(np.isnan(x), 0.0, np.abs(x).astype(np.float64))  # NaN is coded at the end
+    e = np.clip(np.floor(np.log2(np.maximum(a, 2.0**-12))), -6, 8)
+    step = 2.0 ** (e - 3)
+    r = np.minimum(np.rint(a / step) * step, 448.0)
+    # value -> code: exponent field and mantissa from the rounded magnitude
+    re = np.where(r >= 2.0**-6, np.floor(np.log2(np.maximum(r, 2.0**-6))), -7)
+    mant = np.where(re >= -6, np.rint((r / 2.0**re - 1.0) * 8.0), np.rint(r / 2.0**-9))
+    exp_field = np.where(re >= -6, re + 7, 0)
+    code = (exp_field.astype(np.int64) << 3) | mant.astype(np.int64)
+    code = np.where(np.signbit(x), code | 0x80, code)
+    code = np.where(np.isnan(x), 0x7F, code)
+    return code.astype(np.uint8)
+
+
+def paged_decode_attention_fp8(
+    q: np.ndarray,
+    k_codes: np.ndarray,
+    v_codes: np.ndarray,
+    k_scale: np.ndarray,
+    v_scale: np.ndarray,
+    block_table: np.ndarray,
+    seq_lens: np.ndarray,
+    scale: float | None = None,
+    dtype: str = "f32",
+) -> np.ndarray:
+    """Decode attention over an e4m3 cache: dequantise (code value * per-KV-head scale), then
+    kernel-lab's fp32 reference math (paged_decode_attention above)."""
+    k = e4m3_decode(k_codes) * np.asarray(k_scale, np.float32)[None, None, :, None]
+    v = e4m3_decode(v_codes) * np.asarray(v_scale, np.float32)[None, None, :, None]
+    return paged_decode_attention(q, k, v, block_table, seq_lens, scale, dtype)
+
+
+def paged_kv_append_fp8(
+    k_codes: np.ndarray,
+    v_codes: np.ndarray,
+    k_new: np.ndarray,
+    v_new: np.ndarray,
+    k_scale: np.ndarray,
+    v_scale: np.ndarray,
+    block_table: np.ndarray,
+    positions: np.ndarray,
+) -> tuple[np.ndarray, np.ndarray, int]:
+    """paged_kv_append into an e4m3 cache: each new row is quantised per KV head,
+    e4m3(x / scale) with the division done in float32, then scattered like paged_kv_append."""
+    ks = np.asarray(k_scale, np.float32)[None, :, None]
+    vs = np.asarray(v_scale, np.float32)[None, :, None]
+    hkv, d = k_codes.shape[2], k_codes.shape[3]
+    kq = e4m3_encode((np.asarray(k_new, np.float32).reshape(-1, hkv, d) / ks).astype(np.float32))
+    vq = e4m3_encode((np.asarray(v_new, np.float32).reshape(-1, hkv, d) / vs).astype(np.float32))
+    return paged_kv_append(k_codes, v_codes, kq, vq, block_table, positions)
+
 
 def paged_kv_append(
     k_cache: np.ndarray,

@@ -38,6 +38,8 @@ def test_header_declares_the_abi():
         "kl_paged_decode_read_status",
         "kl_paged_decode_noalloc",
         "kl_paged_kv_append",
+        "kl_paged_decode_fp8",
+        "kl_paged_kv_append_fp8",
     ]
 
 
@@ -105,6 +107,8 @@ def test_torch_ops_have_the_reference_schemas():
         op = getattr(torch.ops.kernel_lab, name)
         assert str(op.default._schema) == str(torch._C.parse_schema("kernel_lab::" + schema))
     assert "num_splits" in str(torch.ops.kernel_lab.paged_decode_attention_splits.default._schema)
+    for name in ("paged_decode_attention_fp8", "paged_kv_append_fp8"):
+        assert "k_scale" in str(getattr(torch.ops.kernel_lab, name).default._schema)
     assert str(torch.ops.kernel_lab.paged_kv_append.default._schema) == str(torch._C.parse_schema(
         "kernel_lab::paged_kv_append(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, "
         "Tensor block_table, Tensor positions) -> ()"))

@@ -170,3 +170,40 @@ def test_append_oracle_rebuilds_the_fixture_pool_token_by_token():
                                            np.array([0, -1, -1, -1, 16 * bt.shape[1]], np.int32))
     assert status == oracle.KL_STATUS_BAD_PAGE
     np.testing.assert_array_equal(k2, k)  # both writes skipped
+
+
+def test_e4m3_codec_is_pinned_to_torch_float8():
+    """The oracle's e4m3 codec against torch.float8_e4m3fn: every code decodes to the same value;
+    encoding rounds to nearest-even exactly as torch wherever torch's result is finite (|x| <
+    464); beyond that the oracle saturates to +-448 (the kernels' saturate-finite rounding,
+    which torch's cast does not do) and NaN stays NaN."""
+    import torch
+
+    codes = np.arange(256, dtype=np.uint8)
+    want = torch.from_numpy(codes.copy()).view(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(oracle.e4m3_decode(codes), want)
+    rng = np.random.default_rng(7)
+    x = np.concatenate([rng.standard_normal(50_000).astype(np.float32) * s for s in (1e-3, 0.05, 1.0, 30.0, 200.0)])
+    x = np.concatenate([x, oracle.E4M3_VALUES[np.isfinite(oracle.E4M3_VALUES)]])
+    x = x[np.abs(x) < 464]
+    torch_codes = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(oracle.e4m3_encode(x), torch_codes)
+    sat = oracle.e4m3_decode(oracle.e4m3_encode(np.array([470.0, 1e6, -1e6, np.nan], np.float32)))
+    assert sat[:3].tolist() == [448.0, 448.0, -448.0] and np.isnan(sat[3])
+
+
+def test_fp8_append_oracle_quantises_then_scatters():
+    hkv, d = 2, 8
+    k_codes = np.zeros((3, 4, hkv, d), np.uint8)
+    bt = np.array([[2, 0], [1, 0]], np.int32)
+    k_new = np.linspace(-3, 3, 2 * hkv * d, dtype=np.float32).reshape(2, hkv, d)
+    k_new[0, 1, 3] = 7.0  # 7 / 0.01 = 700 > 448: saturates
+    scale = np.array([0.5, 0.01], np.float32)
+    k2, v2, status = oracle.paged_kv_append_fp8(k_codes, k_codes, k_new, k_new, scale, scale, bt,
+                                                np.array([5, -1], np.int32))
+    assert status == 0
+    # position 5 of sequence 0: page bt[0, 1] = 0, slot 1; one head-1 value saturates
+    got = oracle.e4m3_decode(k2[0, 1]) * scale[:, None]
+    np.testing.assert_allclose(got[0], k_new[0, 0], rtol=2**-3)
+    assert oracle.e4m3_decode(k2[0, 1, 1])[3] == 448.0
+    assert (k2[1:] == 0).all() and (k2[0, 0] == 0).all()
