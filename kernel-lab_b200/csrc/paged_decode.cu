@@ -805,20 +805,23 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
         for (int mt = 0; mt < OW / 2; ++mt) {
           // m-tile c*OW/2 + mt: row g holds d = 8*OW*c + OW*g + 2mt (the lane's output value 2mt
           // of piece c), row g + 8 holds d + 1; columns are tokens 2t4, 2t4+1, 2t4+8, 2t4+9.
-          uint32_t w0, w1, w2, w3;
+          uint32_t a0, a1, a2, a3;
           if constexpr (!KV8) {
-            w0 = va[mt], w1 = vb[mt], w2 = vc[mt], w3 = vd[mt];
+            a0 = __byte_perm(va[mt], vb[mt], 0x5410);
+            a1 = __byte_perm(va[mt], vb[mt], 0x7632);
+            a2 = __byte_perm(vc[mt], vd[mt], 0x5410);
+            a3 = __byte_perm(vc[mt], vd[mt], 0x7632);
           } else {
-            const int sh = (mt & 1) * 16;
-            w0 = e4m3x2_to_f16x2(va[mt >> 1] >> sh);
-            w1 = e4m3x2_to_f16x2(vb[mt >> 1] >> sh);
-            w2 = e4m3x2_to_f16x2(vc[mt >> 1] >> sh);
-            w3 = e4m3x2_to_f16x2(vd[mt >> 1] >> sh);
+            // Pair the two tokens' bytes first, (tok0 d, tok1 d, tok0 d+1, tok1 d+1); one
+            // conversion per register then yields the fragment.
+            const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+            const uint32_t x01 = __byte_perm(va[mt >> 1], vb[mt >> 1], sel);
+            const uint32_t x23 = __byte_perm(vc[mt >> 1], vd[mt >> 1], sel);
+            a0 = e4m3x2_to_f16x2(x01);
+            a1 = e4m3x2_to_f16x2(x01 >> 16);
+            a2 = e4m3x2_to_f16x2(x23);
+            a3 = e4m3x2_to_f16x2(x23 >> 16);
           }
-          const uint32_t a0 = __byte_perm(w0, w1, 0x5410);
-          const uint32_t a1 = __byte_perm(w0, w1, 0x7632);
-          const uint32_t a2 = __byte_perm(w2, w3, 0x5410);
-          const uint32_t a3 = __byte_perm(w2, w3, 0x7632);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             Mma<MT>::run(acc[c * (OW / 2) + mt][nt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
