@@ -11,7 +11,8 @@ heads (32 query / 8 KV, head_dim 128, 16-token pages), bf16, batch 64, context 4
 shuffled pages, NaN-poisoned spare pages. A step is one decode call. At N GPUs the batch
 grows to 64*N and every rank decodes its own 64 sequences with every head: sequences are
 independent, so there is no collective, and every GPU streams the same 1.07 GB of KV per
-step (weak scaling). ``decode70b``: Llama-3-70B heads (64/8), batch 256, context 8192,
+step (weak scaling). ``decode_fp8``: the same with an e4m3 KV cache (per-KV-head scales; KV
+bytes counted at one per element). ``decode70b``: Llama-3-70B heads (64/8), batch 256, context 8192,
 total work fixed across N (strong scaling) in the tensor-parallel layout: KV heads sharded
 N ways and the outputs all-gathered with NCCL inside the step. ``rmsnorm``: fused add +
 RMSNorm, 4096 x 8192 bf16.
@@ -41,6 +42,7 @@ sys.path[:0] = [str(REPO), str(REPO / "kernel-lab_b200")]
 
 METRIC = "paged decode attn % of B200 peak HBM BW (Llama-3-8B GQA bs64 ctx4096); us/call"
 RMS_METRIC = "fused add+RMSNorm % of B200 peak HBM BW (4096 tokens x 8192 hidden, bf16); us/call"
+FP8_METRIC = "paged decode attn, e4m3 KV cache, algorithmic HBM GB/s (Llama-3-8B GQA bs64 ctx4096); us/call"
 L2_NOTE = "inputs larger than L2 (no flush needed)"
 
 
@@ -50,7 +52,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "ours", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["decode", "decode70b", "rmsnorm"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "decode_fp8", "decode70b", "rmsnorm"], default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, help="override the workload's batch (per GPU for weak scaling)")
@@ -64,6 +66,12 @@ def workload_spec(name: str, world: int) -> dict:
         return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
                     layout="sequences",
                     desc="paged decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU, ctx 4096")
+    if name == "decode_fp8":
+        # The headline with an e4m3 KV cache (per-KV-head scales): half the KV bytes per token.
+        return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
+                    layout="sequences", kv8=True,
+                    desc="paged decode, e4m3 KV cache, Llama-3-8B heads 32/8/128, page 16, bf16 q/out, "
+                         "batch 64/GPU, ctx 4096")
     if name == "decode70b":
         # Tensor-parallel layout: KV heads sharded, one all-gather of the outputs per step.
         return dict(kind="decode", batch=256, ctx=8192, hq=64, hkv=8, d=128, page=16, scaling="strong",
@@ -297,19 +305,34 @@ def main() -> None:
         scale = d**-0.5
         out_local = torch.empty_like(q)
         out_full = torch.empty((B, hq, d), dtype=q.dtype, device=dev) if gather else None
-        kernel_work = decode_attention_work([ctx] * b_local, hq_l, hkv_l, d, 2)  # per rank, per launch
-        job_bytes = decode_attention_work([ctx] * B, hq, hkv, d, 2).bytes
+        kv_bytes = 1 if spec.get("kv8") else 2
+        kernel_work = decode_attention_work([ctx] * b_local, hq_l, hkv_l, d, 2, kv_bytes)  # per rank, per launch
+        job_bytes = decode_attention_work([ctx] * B, hq, hkv, d, 2, kv_bytes).bytes
+        if spec.get("kv8"):
+            from kernel_lab.kv_cache import e4m3_scales, quantize_e4m3
+
+            k_scale, v_scale = e4m3_scales(kv.k_cache), e4m3_scales(kv.v_cache)
+            k8, v8 = quantize_e4m3(kv.k_cache, k_scale), quantize_e4m3(kv.v_cache, v_scale)
+            kv = type(kv)(k8, v8, kv.block_table, kv.seq_lens, kv.page_size)
+            torch.cuda.empty_cache()
+
+            def decode_op(out_t, q_t, bt_t, ln_t):
+                torch.ops.kernel_lab.paged_decode_attention_fp8(out_t, q_t, kv.k_cache, kv.v_cache, k_scale, v_scale,
+                                                                bt_t, ln_t, scale)
+        else:
+
+            def decode_op(out_t, q_t, bt_t, ln_t):
+                torch.ops.kernel_lab.paged_decode_attention(out_t, q_t, kv.k_cache, kv.v_cache, bt_t, ln_t, scale)
 
         def kernel():
-            torch.ops.kernel_lab.paged_decode_attention(out_local, q, kv.k_cache, kv.v_cache, kv.block_table,
-                                                        kv.seq_lens, scale)
+            decode_op(out_local, q, kv.block_table, kv.seq_lens)
 
         def step():
             kernel()
             if gather:
                 gather_heads(out_local, world, out=out_full)
 
-        metric = METRIC
+        metric = FP8_METRIC if spec.get("kv8") else METRIC
     else:
         R, H = spec["rows"], spec["hidden"]
         g = torch.Generator(device=dev).manual_seed(7)
@@ -402,8 +425,7 @@ def main() -> None:
             stream.wait_event(arrived)
             if sl["out_read"] is not None:
                 stream.wait_event(sl["out_read"])  # the copy-out two steps back has read the slot
-            torch.ops.kernel_lab.paged_decode_attention(sl["out"], sl["q"], kv.k_cache, kv.v_cache, sl["bt"],
-                                                        sl["ln"], scale)
+            decode_op(sl["out"], sl["q"], sl["bt"], sl["ln"])
             src = gather_heads(sl["out"], world, out=sl["full"]) if gather else sl["out"]
             done = torch.cuda.Event()
             done.record(stream)
@@ -473,7 +495,7 @@ def main() -> None:
         traffic = load_traffic(key)
         value = job_bytes / (step_ms * 1e-3) / 1e9
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not spec.get("kv8"):  # kernel-lab has no e4m3 path
             cpu = cpu_measure(spec["kind"], spec, args.cpu_seconds)
         layout = spec.get("layout")
         parallelism = "1 gpu" if world == 1 else f"kv-head tp{world}" if layout == "kv_heads" else f"sequences dp{world}"

@@ -44,11 +44,13 @@ def rms_norm_work(rows: int, hidden: int, elem_bytes: int, fused_residual: bool)
 
 
 def decode_attention_work(
-    seq_lens: list[int], num_q_heads: int, num_kv_heads: int, head_dim: int, elem_bytes: int
+    seq_lens: list[int], num_q_heads: int, num_kv_heads: int, head_dim: int, elem_bytes: int,
+    kv_elem_bytes: int | None = None,
 ) -> Work:
-    """K and V of every cached token once, q read and out written once; 4*D FLOPs per (head, token)."""
+    """K and V of every cached token once, q read and out written once; 4*D FLOPs per (head, token).
+    ``kv_elem_bytes`` (default ``elem_bytes``) is the cache's element size: 1 for an e4m3 cache."""
     tokens = sum(max(int(n), 0) for n in seq_lens)
-    kv = 2 * tokens * num_kv_heads * head_dim * elem_bytes
+    kv = 2 * tokens * num_kv_heads * head_dim * (elem_bytes if kv_elem_bytes is None else kv_elem_bytes)
     q_out = 2 * len(seq_lens) * num_q_heads * head_dim * elem_bytes
     return Work(bytes=kv + q_out, flops=4 * tokens * num_q_heads * head_dim)
 
