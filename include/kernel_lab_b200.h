@@ -39,7 +39,8 @@ enum {
 enum {
   KL_STATUS_BAD_PAGE = 1,     /* a block-table entry outside [0, num_pages): that page was skipped */
   KL_STATUS_LEN_CLAMPED = 2,  /* a sequence longer than max_pages_per_seq * page_size was clamped */
-  KL_STATUS_WAIT_TIMEOUT = 4  /* an internal pipeline wait exceeded its time limit; output is invalid */
+  KL_STATUS_WAIT_TIMEOUT = 4,  /* an internal pipeline wait exceeded its time limit; output is invalid */
+  KL_STATUS_BAD_PREFIX_GROUPS = 8  /* cascade: prefix_indptr is not a partition of the batch; prefixes ignored */
 };
 
 /* Library version string, e.g. "kernel_lab_b200 0.1.0 sm_100a". */
@@ -189,6 +190,38 @@ int kl_paged_kv_append_fp8(int dtype, void* k_cache, void* v_cache, const void* 
                            const int32_t* positions, int batch, int num_kv_heads, int head_dim, int page_size,
                            int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
                            int64_t new_row_stride, uint32_t* status, void* stream);
+
+/*
+ * Cascade (shared-prefix) decode: the sequences of group p, [prefix_indptr[p], prefix_indptr[p+1]),
+ * share the prefix_lens[p] tokens held in the pages of row p of prefix_block_table
+ * ([num_prefixes, >= max_prefix_pages] int32, rows prefix_block_table_stride apart, pages of the
+ * same pools). Sequence b attends to its group's prefix tokens and then to its own
+ * seq_lens[b] tokens (block_table row b):
+ *   out[b, h] = softmax(scale * q[b, h] . [K_prefix(b); K_b]^T) [V_prefix(b); V_b].
+ * A prefix's pages are read once per block of sequences of its group (the block's query rows
+ * share each tensor-core MMA), not once per sequence, and the two parts are merged exactly by
+ * their log-sum-exp in the same launch. prefix_indptr must partition the batch (entry 0 = 0,
+ * non-decreasing, entry num_prefixes = batch); otherwise the prefixes are ignored and
+ * KL_STATUS_BAD_PREFIX_GROUPS is set. num_prefixes == 0 is plain kl_paged_decode. k_scale and
+ * v_scale both NULL: caches of `dtype`; both given: e4m3 caches as in kl_paged_decode_fp8.
+ * Tensor-core shapes only (fp16/bf16, head_dim 64/128/256, page size 8 or a multiple of 16);
+ * other shapes return cudaErrorInvalidValue. Scratch from
+ * kl_paged_decode_cascade_workspace_size, with the same rules as kl_paged_decode's.
+ * Mirrors FlashInfer's two-level cascade (shared prefix + unique suffix), which kernel-lab names
+ * as a next step (docs/design.md:96-102); no counterpart in kernel-lab.
+ */
+int kl_paged_decode_cascade_workspace_size(int dtype, int batch, int num_prefixes, int num_q_heads,
+                                           int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+                                           int max_prefix_pages, size_t* partial_bytes, size_t* sync_bytes);
+
+int kl_paged_decode_cascade(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                            const float* k_scale, const float* v_scale, const int32_t* prefix_block_table,
+                            const int32_t* prefix_lens, const int32_t* prefix_indptr, int num_prefixes,
+                            int64_t prefix_block_table_stride, int max_prefix_pages, const int32_t* block_table,
+                            const int32_t* seq_lens, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                            int page_size, int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
+                            float scale, void* partials, size_t partial_bytes, void* sync, size_t sync_bytes,
+                            void* stream);
 
 #ifdef __cplusplus
 }

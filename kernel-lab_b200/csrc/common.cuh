@@ -101,6 +101,7 @@ enum StatusBits : uint32_t {
   kStatusBadPage = 1u,       // a block-table entry outside [0, num_pages): that page was skipped
   kStatusLenClamped = 2u,    // a sequence longer than max_pages * page_size was clamped
   kStatusWaitTimeout = 4u,   // an mbarrier wait ran out of time; the kernel stopped early
+  kStatusBadPrefixGroups = 8u,  // cascade groups do not partition the batch: prefixes were ignored
 };
 
 // ----------------------------------------------------------------- shared-memory addresses
@@ -218,6 +219,13 @@ __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_re
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// L2 policy for data that other CTAs read again soon (a shared prefix's pages).
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 

@@ -94,6 +94,18 @@ struct DecodeArgs {
   float* part_lse;      // [slot][slot_heads]
   const float* k_scale;  // e4m3 cache: per-KV-head dequantisation scales (null otherwise)
   const float* v_scale;
+  // Cascade (shared-prefix) decode; off when num_prefixes == 0. The sequences of group p,
+  // [prefix_indptr[p], prefix_indptr[p+1]), share prefix_lens[p] tokens held in the pages of row p
+  // of prefix_bt; each sequence attends to them and to its own tokens (block_table, seq_lens).
+  const int32_t* prefix_bt;
+  const int32_t* prefix_lens;
+  const int32_t* prefix_indptr;
+  int num_prefixes;
+  int64_t prefix_bt_stride;
+  int prefix_max_pages;
+  int members;    // sequences whose query rows one prefix item packs (a "member block")
+  float* cas_o;   // [2][batch * num_q_heads][head_dim]: normalised output of each side (0: prefix)
+  float* cas_lse; // [2][batch * num_q_heads]: base-2 LSE of each side
 };
 
 struct TcShape {
@@ -112,21 +124,43 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // ------------------------------------------------------------------------- plan
 
+// Plan entries: without a cascade, entry b is sequence b. With one, entries [0, V) are prefix
+// items (member blocks: up to `members` consecutive sequences of one group, whose query rows
+// share each MMA) and entry V + b is sequence b's own tokens.
 struct Seg {
-  int b, u;                // sequence, unit
+  int b, u;                // plan entry, unit
   int tok_begin, tok_end;  // token range; empty when tok_end <= tok_begin
   int chunk;               // chunk id of this piece (partial slots derive from it)
-  int nchunks;             // chunks of this (sequence, unit)
+  int nchunks;             // chunks of this (entry, unit)
   int c_first;             // balanced mode: CTA holding the first chunk
   bool first_aligned;      // balanced mode: the first chunk starts its CTA's range
   bool whole;
+  int seq;                 // first sequence whose query rows the entry serves
+  int nmem;                // sequences it serves (1 unless a prefix item)
+  int grp;                 // prefix group of a prefix item, -1 for a sequence's own tokens
+  int cb;                  // arrival-counter block: seq for own tokens, batch + entry for prefix items
 };
 
 struct Walk {
   int t, t1, R;     // balanced
   bool first;       // balanced: no segment produced yet
   int item, items;  // forced
+  int n, V;         // plan entries, prefix items among them
 };
+
+// Shared-memory plan arrays. lens/prefix have one slot per entry (+1 for prefix); hp and vstart
+// exist only for a cascade: hp[b] = clamped prefix length of sequence b's group, vstart[p] = first
+// entry of group p (vstart[num_prefixes] = V).
+struct PlanSmem {
+  int* lens;
+  int* prefix;
+  int* misc;
+  int* hp;
+  int* vstart;
+};
+
+// misc[]: 0 total cost, 1 R, 2 abort flag, 3 spare, 8..40 scan scratch, 48 V, 49 entries.
+constexpr int kMiscScan = 8, kMiscV = 48, kMiscEntries = 49;
 
 __device__ __forceinline__ int clamp_len(const DecodeArgs& a, int b, bool report) {
   int len = a.seq_lens[b];
@@ -138,63 +172,139 @@ __device__ __forceinline__ int clamp_len(const DecodeArgs& a, int b, bool report
   return len < 0 ? 0 : len;
 }
 
-// All threads of the block. lens[b] = clamped length; prefix[b] = cost of one unit of every
-// sequence before b, where a non-empty sequence costs its tiles plus seg_cost (the time a
-// CTA spends starting a (sequence, unit): Q loads, partial write and count, merge);
-// misc[0] = total cost over all units, misc[1] = R; misc[2] (abort flag) and misc[3] are
-// zeroed; misc[4..35] is scan scratch. Ends with a block barrier.
-__device__ void plan_build(const DecodeArgs& a, int* lens, int* prefix, int* misc) {
-  const int B = a.batch;
-  const int nt = blockDim.x;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
-  const int per = (B + nt - 1) / nt;
-  const int lo = min(B, tid * per), hi = min(B, lo + per);
-  int local = 0;
-  for (int i = lo; i < hi; ++i) {
-    const int len = clamp_len(a, i, blockIdx.x == 0);
-    lens[i] = len;
-    local += len > 0 ? (len + kTile - 1) / kTile + a.seg_cost : 0;
+__device__ __forceinline__ int clamp_prefix_len(const DecodeArgs& a, int p, bool report) {
+  int len = a.prefix_lens[p];
+  const int cap = a.prefix_max_pages * a.page_size;
+  if (len > cap) {
+    if (report) atomicOr(a.sync, kStatusLenClamped);
+    len = cap;
   }
+  return len < 0 ? 0 : len;
+}
+
+// Exclusive prefix sum of f(i) over i in [0, n) into out[0..n] (out[n] = total), by every thread
+// of the block; returns the total. Each thread scans a contiguous range, then one warp scans the
+// warps' sums. scratch: 33 ints. Ends with a block barrier.
+template <typename F>
+__device__ int block_scan(int n, F f, int* out, int* scratch) {
+  const int nt = blockDim.x, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+  const int per = (n + nt - 1) / nt;
+  const int lo = min(n, tid * per), hi = min(n, lo + per);
+  int local = 0;
+  for (int i = lo; i < hi; ++i) local += f(i);
   int inc = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xffffffffu, inc, o);
     if (lane >= o) inc += v;
   }
-  int* wtot = misc + 4;
-  if (lane == 31) wtot[warp] = inc;
+  if (lane == 31) scratch[warp] = inc;
   __syncthreads();
   if (warp == 0) {
-    const int v = lane < nw ? wtot[lane] : 0;
+    const int v = lane < nw ? scratch[lane] : 0;
     int vi = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int u = __shfl_up_sync(0xffffffffu, vi, o);
       if (lane >= o) vi += u;
     }
-    if (lane < nw) wtot[lane] = vi - v;
-    if (lane == 31) misc[2] = vi;  // tiles of one unit, all sequences
+    if (lane < nw) scratch[lane] = vi - v;
+    if (lane == 31) scratch[32] = vi;
   }
   __syncthreads();
-  int run = wtot[warp] + inc - local;
+  int run = scratch[warp] + inc - local;
   for (int i = lo; i < hi; ++i) {
-    prefix[i] = run;
-    run += lens[i] > 0 ? (lens[i] + kTile - 1) / kTile + a.seg_cost : 0;
+    out[i] = run;
+    run += f(i);
   }
+  const int total = scratch[32];
+  if (tid == 0) out[n] = total;
+  __syncthreads();
+  return total;
+}
+
+// Group of prefix item e (< V): the last group whose first entry is <= e.
+__device__ __forceinline__ int group_of_entry(const int* vstart, int P, int e) {
+  int lo = 0, hi = P - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (vstart[mid] <= e) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// All threads of the block. Builds the plan's entries: lens[e] = clamped token count, prefix[e] =
+// cost of one unit of every entry before e, where a non-empty entry costs its tiles plus seg_cost
+// (the time a CTA spends starting an (entry, unit): Q loads, partial write and count, merge);
+// misc[0] = total cost over all units, misc[1] = R, misc[2] (abort flag) and misc[3] zeroed,
+// misc[kMiscV] = V, misc[kMiscEntries] = entries. For a cascade, also hp and vstart; a group
+// table that is not a partition of the batch (indptr[0] = 0, non-decreasing, indptr[P] = batch)
+// turns the prefixes off and sets KL_STATUS_BAD_PREFIX_GROUPS. Ends with a block barrier.
+__device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps) {
+  const int B = a.batch;
+  const int nt = blockDim.x, tid = threadIdx.x;
+  const bool report = blockIdx.x == 0;
+  int* misc = ps.misc;
+  int V = 0;
+  if (a.num_prefixes > 0) {
+    const int P = a.num_prefixes, Mb = a.members;
+    bool bad = false;
+    for (int p = tid; p < P; p += nt) {
+      const int lo = __ldg(a.prefix_indptr + p), hi = __ldg(a.prefix_indptr + p + 1);
+      bad |= lo > hi || (p == 0 && lo != 0) || (p == P - 1 && hi != B);
+    }
+    bad = __syncthreads_or(bad);
+    if (bad && report && tid == 0) atomicOr(a.sync, kStatusBadPrefixGroups);
+    V = block_scan(
+        P,
+        [&](int p) {
+          if (bad) return 0;
+          const int m = __ldg(a.prefix_indptr + p + 1) - __ldg(a.prefix_indptr + p);
+          return (m + Mb - 1) / Mb;
+        },
+        ps.vstart, misc + kMiscScan);
+    for (int b = tid; b < B; b += nt) {
+      int len = 0;
+      if (!bad) {
+        int lo = 0, hi = P - 1;  // last group starting at or before b
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (__ldg(a.prefix_indptr + mid) <= b) lo = mid; else hi = mid - 1;
+        }
+        len = clamp_prefix_len(a, lo, false);
+      }
+      ps.hp[b] = len;
+    }
+    if (report) {
+      for (int p = tid; p < P; p += nt) clamp_prefix_len(a, p, true);
+    }
+  }
+  const int n = V + B;
+  for (int e = tid; e < n; e += nt) {
+    ps.lens[e] = e < V ? clamp_prefix_len(a, group_of_entry(ps.vstart, a.num_prefixes, e), false)
+                       : clamp_len(a, e - V, report);
+  }
+  __syncthreads();
+  const int* lens = ps.lens;
+  const int per_unit = block_scan(
+      n, [&](int e) { return lens[e] > 0 ? (lens[e] + kTile - 1) / kTile + a.seg_cost : 0; }, ps.prefix,
+      misc + kMiscScan);
   if (tid == 0) {
-    const int per_unit = misc[2];
-    prefix[B] = per_unit;
     const int total = per_unit * a.units;
     misc[0] = total;
     misc[1] = max(a.min_tiles, (total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x));
     misc[2] = 0;
     misc[3] = 0;
+    misc[kMiscV] = V;
+    misc[kMiscEntries] = n;
   }
   __syncthreads();
 }
 
 __device__ __forceinline__ void walk_init(const DecodeArgs& a, const int* misc, Walk& w) {
+  w.V = misc[kMiscV];
+  w.n = misc[kMiscEntries];
   if (a.splits == 0) {
     const int total = misc[0];
     w.R = misc[1];
@@ -208,17 +318,43 @@ __device__ __forceinline__ void walk_init(const DecodeArgs& a, const int* misc, 
   }
 }
 
-__device__ __forceinline__ bool walk_next(const DecodeArgs& a, const int* lens, const int* prefix, Walk& w,
-                                          Seg& s) {
+// Who entry b serves: a prefix item's member block, or sequence b - V. CAS: the launch is a
+// cascade (otherwise entries are sequences, known at compile time).
+template <bool CAS>
+__device__ __forceinline__ void entry_members(const DecodeArgs& a, const PlanSmem& ps, const Walk& w, Seg& s) {
+  if (!CAS) {
+    s.seq = s.b;
+    s.nmem = 1;
+    s.grp = -1;
+    s.cb = s.b;
+  } else if (s.b < w.V) {
+    const int p = group_of_entry(ps.vstart, a.num_prefixes, s.b);
+    const int first = __ldg(a.prefix_indptr + p), end = __ldg(a.prefix_indptr + p + 1);
+    s.seq = first + (s.b - ps.vstart[p]) * a.members;
+    s.nmem = min(a.members, end - s.seq);
+    s.grp = p;
+    s.cb = a.batch + s.b;
+  } else {
+    s.seq = s.b - w.V;
+    s.nmem = 1;
+    s.grp = -1;
+    s.cb = s.seq;
+  }
+}
+
+template <bool CAS = false>
+__device__ __forceinline__ bool walk_next(const DecodeArgs& a, const PlanSmem& ps, Walk& w, Seg& s) {
   const int U = a.units;
+  const int* lens = ps.lens;
+  const int* prefix = ps.prefix;
   if (a.splits == 0) {
     if (w.t >= w.t1) return false;
-    int lo = 0, hi = a.batch - 1;  // largest b with U * prefix[b] <= t
+    int lo = 0, hi = w.n - 1;  // largest entry b with U * prefix[b] <= t
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (static_cast<int64_t>(U) * prefix[mid] <= w.t) lo = mid; else hi = mid - 1;
     }
-    // b is never empty here: an empty sequence has the same prefix as the next one.
+    // b is never empty here: an empty entry has the same prefix as the next one.
     const int b = lo;
     const int nc = prefix[b + 1] - prefix[b];      // cost of one unit: seg_cost, then the tiles
     const int n = (lens[b] + kTile - 1) / kTile;  // tiles of one unit
@@ -243,6 +379,7 @@ __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const int* lens, 
     s.chunk = w.first ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
     w.first = false;
     w.t = from + len;
+    entry_members<CAS>(a, ps, w, s);
     return true;
   }
   if (w.item >= w.items) return false;
@@ -260,10 +397,11 @@ __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const int* lens, 
   s.first_aligned = true;
   s.whole = S == 1;
   w.item += gridDim.x;
+  entry_members<CAS>(a, ps, w, s);
   return true;
 }
 
-// Chunk id of the k-th chunk of segment s's (sequence, unit).
+// Chunk id of the k-th chunk of segment s's (entry, unit).
 __device__ __forceinline__ int chunk_id(const DecodeArgs& a, const Seg& s, int k) {
   if (a.splits == 0) {
     const int c = s.c_first + k;
@@ -272,23 +410,47 @@ __device__ __forceinline__ int chunk_id(const DecodeArgs& a, const Seg& s, int k
   return (s.b * a.splits + k) * a.units + s.u;
 }
 
-__device__ __forceinline__ uint32_t* counter_of(const DecodeArgs& a, int b, int kvh, int hg) {
-  return a.sync + 1 + (static_cast<int64_t>(b) * a.num_kv_heads + kvh) * kMaxHeadGroups + hg;
+// Arrival counters: block cb in [0, batch) for sequences' own tokens, [batch, 2 batch) for
+// prefix items; a cascade's per-sequence side counters follow at 2 batch + b.
+__device__ __forceinline__ uint32_t* counter_of(const DecodeArgs& a, int cb, int kvh, int hg) {
+  return a.sync + 1 + (static_cast<int64_t>(cb) * a.num_kv_heads + kvh) * kMaxHeadGroups + hg;
 }
 
-// Zero the outputs of empty sequences (balanced mode has no work for them).
+// Zero the outputs of sequences with no token at all (balanced mode has no work for them).
+// seq_len_s[b] = sequence b's own clamped length; hp (cascade only) its group's prefix length.
 template <typename T>
-__device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const int* lens, int ctid, int nthr) {
+__device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const int* seq_len_s, const int* hp,
+                                                     int ctid, int nthr) {
   if (a.splits != 0) return;
   T* out = static_cast<T*>(a.out);
   const int n = a.num_q_heads * a.head_dim;
   for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {
-    if (lens[b] != 0) continue;
+    if (seq_len_s[b] != 0 || (hp != nullptr && hp[b] != 0)) continue;
     for (int i = ctid; i < n; i += nthr) out[static_cast<int64_t>(b) * n + i] = Storage<T>::store(0.0f);
   }
 }
 
-// Merge of a split (sequence, unit, query-head group) by one warp, every chunk's normalised
+// Where a warp's final rows go. Row hl of the warp is query row r = row0 + hl of its entry:
+// member m = r / group, query head kvh * group + r % group of sequence seq + m (rows with
+// m >= nmem are padding). Members whose bit is set in `cas` are one side of a cascade: their rows
+// go, normalised, to that side's fp32 state with their LSE; the other rows are final outputs.
+struct RowSink {
+  int seq, nmem, kvh, row0, side;
+  uint32_t cas;
+};
+
+template <bool CAS>
+__device__ __forceinline__ int64_t sink_row(const DecodeArgs& a, const RowSink& k, int hl, int& m) {
+  const int r = k.row0 + hl;
+  m = CAS ? r / a.group : 0;  // without a cascade every row < nh belongs to member 0
+  return static_cast<int64_t>(k.seq + m) * a.num_q_heads + k.kvh * a.group + (r - m * a.group);
+}
+
+__device__ __forceinline__ int64_t side_offset(const DecodeArgs& a, int side) {
+  return static_cast<int64_t>(side) * a.batch * a.num_q_heads;
+}
+
+// Merge of a split (entry, unit, query-head group) by one warp, every chunk's normalised
 // partial and base-2 LSE being in scratch. Lane k reads chunk k's LSEs (32 chunks a round);
 // the per-head max M and weight sum W come from fixed-order warp reductions. Then lane L owns
 // float4 i = L + 32*j (j < NE) of the nh x D outputs and accumulates sum_k 2^(lse_k - M) * o_k
@@ -296,9 +458,9 @@ __device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const 
 // chunk's lane. The result depends only on the partials, never on which chunk merges; it is
 // written as out = sum / W (zero where every chunk was empty). kernel-lab's merge formula
 // (triton_kernels/paged_attention.py:150-166).
-template <typename T, int D, int HPW, int NE, int KB>
+template <typename T, int D, int HPW, int NE, int KB, bool CAS>
 __device__ __forceinline__ void merge_chunks_impl(const DecodeArgs& a, const Seg& s, int slots_per_chunk, int mu,
-                                                  int nh, T* out_rows, int lane) {
+                                                  int nh, const RowSink& sink, int lane) {
   constexpr int Q = D / 4;  // float4 per head row
   const int n4 = nh * Q;
   const int nchunks = s.nchunks;
@@ -393,44 +555,111 @@ __device__ __forceinline__ void merge_chunks_impl(const DecodeArgs& a, const Seg
     if (i >= n4) continue;
     const int h_lo = (32 * j) / Q, h_hi = min(HPW - 1, (32 * j + 31) / Q);
     const int h = i / Q;
-    float wsum = 0.0f;
+    float wsum = 0.0f, mh = -INFINITY;
 #pragma unroll
     for (int hh = h_lo; hh <= h_hi; ++hh) {
-      if (h == hh) wsum = W[hh];
+      if (h == hh) {
+        wsum = W[hh];
+        mh = M[hh];
+      }
     }
     const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
-    uint2 pk;
-    pk.x = Storage<T>::pack2(o[j].x * inv, o[j].y * inv);
-    pk.y = Storage<T>::pack2(o[j].z * inv, o[j].w * inv);
-    *reinterpret_cast<uint2*>(out_rows + static_cast<int64_t>(h) * D + 4 * (i - h * Q)) = pk;
+    const int c4 = i - h * Q;
+    int m;
+    const int64_t row = sink_row<CAS>(a, sink, h, m);
+    if (CAS && ((sink.cas >> m) & 1u)) {
+      const int64_t srow = side_offset(a, sink.side) + row;
+      reinterpret_cast<float4*>(a.cas_o + srow * D)[c4] =
+          make_float4(o[j].x * inv, o[j].y * inv, o[j].z * inv, o[j].w * inv);
+      if (c4 == 0) a.cas_lse[srow] = wsum > 0.0f ? mh + __log2f(wsum) : -INFINITY;
+    } else {
+      uint2 pk;
+      pk.x = Storage<T>::pack2(o[j].x * inv, o[j].y * inv);
+      pk.y = Storage<T>::pack2(o[j].z * inv, o[j].w * inv);
+      *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + row * D + 4 * c4) = pk;
+    }
   }
 }
 
 // Picks the per-lane slot count for the group's nh x D outputs: 4, 8 or 16 float4 per lane
 // per chunk, with 4, 2 or 1 chunks' loads in flight (64 registers of loads in each case).
-template <typename T, int D, int HPW>
+template <typename T, int D, int HPW, bool CAS>
 __device__ __forceinline__ void merge_chunks(const DecodeArgs& a, const Seg& s, int slots_per_chunk, int mu, int nh,
-                                             T* out_rows, int lane) {
+                                             const RowSink& sink, int lane) {
   constexpr int Q = D / 4;
   const int n4 = nh * Q;
   if (n4 <= 128) {
-    merge_chunks_impl<T, D, HPW, 4, 4>(a, s, slots_per_chunk, mu, nh, out_rows, lane);
+    merge_chunks_impl<T, D, HPW, 4, 4, CAS>(a, s, slots_per_chunk, mu, nh, sink, lane);
   } else if (HPW * Q > 128 && n4 <= 256) {
-    merge_chunks_impl<T, D, HPW, (HPW * Q > 128 ? 8 : 4), 1>(a, s, slots_per_chunk, mu, nh, out_rows, lane);
+    merge_chunks_impl<T, D, HPW, (HPW * Q > 128 ? 8 : 4), 1, CAS>(a, s, slots_per_chunk, mu, nh, sink, lane);
   } else if (HPW * Q > 256) {
-    merge_chunks_impl<T, D, HPW, (HPW * Q > 256 ? 16 : 4), 1>(a, s, slots_per_chunk, mu, nh, out_rows, lane);
+    merge_chunks_impl<T, D, HPW, (HPW * Q > 256 ? 16 : 4), 1, CAS>(a, s, slots_per_chunk, mu, nh, sink, lane);
+  }
+}
+
+// Final output of sequence b's query heads kvh * group + row0 .. + nh in a cascade, once both
+// sides (its group's shared prefix, its own tokens) have stored their normalised outputs and
+// LSEs: out = (2^(lse0 - M) o0 + 2^(lse1 - M) o1) / (2^(lse0 - M) + 2^(lse1 - M)), M the larger
+// LSE; the same arithmetic whichever side merges. One warp, lane-parallel over float4 columns.
+template <typename T, int D>
+__device__ __forceinline__ void cascade_merge(const DecodeArgs& a, int b, int kvh, int row0, int nh, int lane) {
+  constexpr int Q = D / 4;
+  const int64_t plane = side_offset(a, 1);
+  const int64_t r0 = static_cast<int64_t>(b) * a.num_q_heads + kvh * a.group + row0;
+  T* out = static_cast<T*>(a.out);
+  for (int i = lane; i < nh * Q; i += 32) {
+    const int h = i / Q, c4 = i - h * Q;
+    const int64_t row = r0 + h;
+    const float l0 = __ldcg(a.cas_lse + row), l1 = __ldcg(a.cas_lse + plane + row);
+    const float mx = fmaxf(l0, l1);
+    const float w0 = l0 > -INFINITY ? fast_exp2(l0 - mx) : 0.0f;
+    const float w1 = l1 > -INFINITY ? fast_exp2(l1 - mx) : 0.0f;
+    const float inv = w0 + w1 > 0.0f ? 1.0f / (w0 + w1) : 0.0f;
+    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a.cas_o + row * D) + c4);
+    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a.cas_o + (plane + row) * D) + c4);
+    uint2 pk;
+    pk.x = Storage<T>::pack2((w0 * x0.x + w1 * x1.x) * inv, (w0 * x0.y + w1 * x1.y) * inv);
+    pk.y = Storage<T>::pack2((w0 * x0.z + w1 * x1.z) * inv, (w0 * x0.w + w1 * x1.w) * inv);
+    *reinterpret_cast<uint2*>(out + row * D + 4 * c4) = pk;
+  }
+}
+
+// After a warp has stored one side of a cascade for the members in sink.cas: each such member's
+// lane counts the side's arrival (a release of the warp's stores); the second side to arrive
+// (acquire) merges the member's rows and returns its counter to zero. `hg` is the query-head
+// group of the counter: a member's rows in it are its query heads grow0 .. grow0 + nh of the KV
+// head's group (grow0 = hg * heads per warp; a packed prefix item has one group).
+template <typename T, int D>
+__device__ __forceinline__ void cascade_arrive(const DecodeArgs& a, const RowSink& sink, int hg, int grow0, int nh,
+                                               int lane) {
+  __syncwarp();
+  bool second = false;
+  if (lane < sink.nmem && ((sink.cas >> lane) & 1u)) {
+    second = atom_add_acq_rel_gpu(counter_of(a, 2 * a.batch + sink.seq + lane, sink.kvh, hg), 1u) == 1u;
+  }
+  uint32_t todo = __ballot_sync(0xffffffffu, second);
+  while (todo != 0u) {
+    const int m = __ffs(todo) - 1;
+    todo &= todo - 1u;
+    __syncwarp();
+    cascade_merge<T, D>(a, sink.seq + m, sink.kvh, grow0, nh, lane);
+    if (lane == m) {
+      *reinterpret_cast<volatile uint32_t*>(counter_of(a, 2 * a.batch + sink.seq + m, sink.kvh, hg)) = 0u;
+    }
   }
 }
 
 // ------------------------------------------------------------------------- tensor-core kernel
 
 struct TcLayout {
-  uint32_t head_bytes, half, stage_bytes, ring, bars, red_m, red_l, red_acc, misc, prefix, lens, total;
+  uint32_t head_bytes, half, stage_bytes, ring, bars, red_m, red_l, red_acc, misc, prefix, lens, hp, vstart, total;
 };
 
 __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int nstage, int batch, int eb = 2) {
+// groups > 0: a cascade over that many prefix groups (plan entries for prefix items as well).
+__host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int nstage, int batch, int eb = 2,
+                                              int groups = 0) {
   TcLayout L{};
   L.head_bytes = kTile * D * eb;  // one head's K (or V) rows of a tile (eb bytes per element)
   L.half = HT * L.head_bytes;
@@ -450,15 +679,71 @@ __host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int
   off += red_warps * 8u * NT * (D + 4u) * 4u;
   L.misc = off;
   off += 64u * 4u;
+  const uint32_t entries = groups > 0 ? 2u * batch : static_cast<uint32_t>(batch);
   L.prefix = off;
-  off += (batch + 1u) * 4u;
+  off += (entries + 1u) * 4u;
   L.lens = off;
-  off += batch * 4u;
+  off += entries * 4u;
+  L.hp = off;
+  off += groups > 0 ? batch * 4u : 0u;
+  L.vstart = off;
+  off += groups > 0 ? (groups + 1u) * 4u : 0u;
   L.total = align_up(off, 16) + 1024u;  // slack to align the base to 1024 B (swizzle atom)
   return L;
 }
 
-template <typename T, int D, int NT, bool KV8>
+// Stores a warp's final rows held in the MMA fragment layout: lane (g, t4) owns, for row
+// hl = nt*8 + 2*t4 + e and piece c, output d = 8*OW*c + OW*g + k (k < OW), the value
+// X[c*OW/2 + k/2][nt][e + 2*(k & 1)] * f[nt][e]. Rows hl >= nh are padding. A cascade member's
+// rows go to its side's fp32 state (with lse), the others to out as T.
+template <typename T, int D, int NT, int OW, bool CAS>
+__device__ __forceinline__ void store_rows(const DecodeArgs& a, const RowSink& sink, const float (&X)[D / 16][NT][4],
+                                           const float (&f)[NT][2], const float (&lse)[NT][2], int g, int t4,
+                                           int nh) {
+  constexpr int NCH = D / (8 * OW);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int hl = nt * 8 + 2 * t4 + e;
+      if (hl >= nh) continue;
+      int m;
+      const int64_t row = sink_row<CAS>(a, sink, hl, m);
+      const float x = f[nt][e];
+      if (CAS && ((sink.cas >> m) & 1u)) {
+        const int64_t srow = side_offset(a, sink.side) + row;
+        float* dst = a.cas_o + srow * D;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+          for (int h = 0; h < OW / 4; ++h) {
+            const int m0 = c * (OW / 2) + 2 * h;
+            *reinterpret_cast<float4*>(dst + c * 8 * OW + OW * g + 4 * h) =
+                make_float4(X[m0][nt][e] * x, X[m0][nt][e + 2] * x, X[m0 + 1][nt][e] * x, X[m0 + 1][nt][e + 2] * x);
+          }
+        }
+        if (g == 0) a.cas_lse[srow] = lse[nt][e];
+      } else {
+        T* orow = static_cast<T*>(a.out) + row * D;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+          for (int h = 0; h < OW / 8; ++h) {
+            const int m0 = c * (OW / 2) + 4 * h;
+            uint4 pk;
+            pk.x = Storage<T>::pack2(X[m0 + 0][nt][e] * x, X[m0 + 0][nt][e + 2] * x);
+            pk.y = Storage<T>::pack2(X[m0 + 1][nt][e] * x, X[m0 + 1][nt][e + 2] * x);
+            pk.z = Storage<T>::pack2(X[m0 + 2][nt][e] * x, X[m0 + 2][nt][e + 2] * x);
+            pk.w = Storage<T>::pack2(X[m0 + 3][nt][e] * x, X[m0 + 3][nt][e + 2] * x);
+            *reinterpret_cast<uint4*>(orow + c * 8 * OW + OW * g + 8 * h) = pk;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <typename T, int D, int NT, bool KV8, bool CAS>
 __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                                   const __grid_constant__ CUtensorMap tmv,
                                                                   const DecodeArgs a, const TcShape cfg) {
@@ -474,15 +759,19 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int HT = cfg.ht, HG = cfg.hg, TW = cfg.tw, nstage = cfg.nstage;
-  const TcLayout L = tc_layout(D, NT, HT, TW, nstage, a.batch, EB);
+  const TcLayout L = tc_layout(D, NT, HT, TW, nstage, a.batch, EB, a.num_prefixes);
   const uint32_t ring = smem_u32(smem + L.ring);
   const uint32_t bars = smem_u32(smem + L.bars);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m);
   float* red_l = reinterpret_cast<float*>(smem + L.red_l);
   float* red_acc = reinterpret_cast<float*>(smem + L.red_acc);
-  int* misc = reinterpret_cast<int*>(smem + L.misc);
-  int* prefix = reinterpret_cast<int*>(smem + L.prefix);
-  int* lens = reinterpret_cast<int*>(smem + L.lens);
+  PlanSmem ps;
+  ps.misc = reinterpret_cast<int*>(smem + L.misc);
+  ps.prefix = reinterpret_cast<int*>(smem + L.prefix);
+  ps.lens = reinterpret_cast<int*>(smem + L.lens);
+  ps.hp = a.num_prefixes > 0 ? reinterpret_cast<int*>(smem + L.hp) : nullptr;
+  ps.vstart = a.num_prefixes > 0 ? reinterpret_cast<int*>(smem + L.vstart) : nullptr;
+  int* misc = ps.misc;
   // A stage half holds the tile as rows of 128 bytes, row r = token * HT * NCH + piece with
   // piece = head * NCH + c over the tile's HT heads, in the TMA's 128-byte swizzle: 16-byte unit
   // u of row r sits at unit u ^ (r & 7).
@@ -502,7 +791,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     tma_prefetch_descriptor(&tmk);
     tma_prefetch_descriptor(&tmv);
   }
-  plan_build(a, lens, prefix, misc);
+  plan_build(a, ps);
   volatile int* abort_flag = misc + 2;
 
   if (warp == kCW) {
@@ -517,7 +806,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     walk_init(a, misc, w);
     Seg s;
     uint32_t gt = 0;
-    const uint64_t policy = l2_policy_evict_first();
+    // Pages read once are streamed (evict first); a shared prefix's pages are read again by the
+    // group's other member blocks, so they keep the normal priority.
+    const uint64_t policy_stream = l2_policy_evict_first();
+    const uint64_t policy_shared = l2_policy_evict_normal();
     const int p_rows = cfg.p_rows;
     const int nsub = kTile / p_rows;
     const uint32_t sub_bytes = 2u * p_rows * rows_per_tok * 128u;
@@ -526,11 +818,14 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     // measured faster (batch 256 x 8192 tokens, 70B heads).
     const int batch_max = L.stage_bytes <= kBatchStageBytes ? min(32, nstage) : 1;
     bool ok = true;
-    while (ok && walk_next(a, lens, prefix, w, s)) {
+    while (ok && walk_next<CAS>(a, ps, w, s)) {
       const int ntok = s.tok_end - s.tok_begin;
       if (ntok <= 0) continue;
       const int ntiles = (ntok + kTile - 1) / kTile;
-      const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.b) * a.bt_stride;
+      const bool shared = CAS && s.grp >= 0;
+      const int32_t* bt_row = shared ? a.prefix_bt + static_cast<int64_t>(s.grp) * a.prefix_bt_stride
+                                     : a.block_table + static_cast<int64_t>(s.seq) * a.bt_stride;
+      const uint64_t policy = shared ? policy_shared : policy_stream;
       const int last_page = (s.tok_end - 1) / a.page_size;
       const int piece0 = s.u * rows_per_tok;
       // Block-table window [wbase, wbase + 64): entry wbase + lane in cur, wbase + 32 + lane in nxt.
@@ -630,7 +925,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   // the V loads 4-way shared-memory bank conflicts (every token of a (head, piece) has the
   // same swizzle phase); a piece-major stage with permuted token rows removes them but measured
   // no faster, the kernel being bound by HBM, not shared memory.
-  zero_empty_sequences<T>(a, lens, threadIdx.x, kCW * 32);
+  zero_empty_sequences<T>(a, ps.lens + misc[kMiscV], ps.hp, threadIdx.x, kCW * 32);
   const int ht = warp % HT;
   const int hg = (warp / HT) % HG;
   const int tw = warp / (HT * HG);
@@ -643,7 +938,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   walk_init(a, misc, w);
   Seg s;
   uint32_t gt = 0;
-  while (walk_next(a, lens, prefix, w, s)) {
+  while (walk_next<CAS>(a, ps, w, s)) {
     const int ntok = max(0, s.tok_end - s.tok_begin);
     const int ntiles = (ntok + kTile - 1) / kTile;
     const int kvh = s.u * HT + ht;
@@ -652,17 +947,21 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     // latency hides behind this segment's tiles. If all of them have, this chunk is the last
     // one and merges straight from its registers at the end of the segment.
     uint32_t published = 0;
-    if (!s.whole && tw == 0 && lane == 0) published = ld_relaxed_gpu(counter_of(a, s.b, kvh, hg));
+    if (!s.whole && tw == 0 && lane == 0) published = ld_relaxed_gpu(counter_of(a, s.cb, kvh, hg));
 
     // Q^T as the B operand, in the permuted contraction order of the K loads: one 16-byte load
     // per 32 d (16-bit cache) or two per 64 d (e4m3 cache, converted to f16).
     uint32_t qf[KS][NT][2];
-    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int h = hg * HPW + nt * 8 + g;
-      const bool hv = h < G;
-      const uint4* qrow = reinterpret_cast<const uint4*>(qb + static_cast<int64_t>(hv ? h : 0) * D);
+      // Query row r of the entry: member r / G (a prefix item packs several sequences' rows into
+      // the MMA's N columns), query head r % G of KV head kvh's group.
+      const int r = hg * HPW + nt * 8 + g;
+      const int m = CAS ? r / G : (r < G ? 0 : 1);
+      const bool hv = m < s.nmem;
+      const uint4* qrow = reinterpret_cast<const uint4*>(
+          static_cast<const T*>(a.q) +
+          (static_cast<int64_t>(s.seq + (hv ? m : 0)) * a.num_q_heads + kvh * G + (hv ? r - m * G : 0)) * D);
       if constexpr (!KV8) {
 #pragma unroll
         for (int kk = 0; kk < D / 32; ++kk) {
@@ -915,32 +1214,34 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     }
 
     // ---- emit: the final output, or this chunk's partial and (if last) the merge.
-    T* out = static_cast<T*>(a.out);
-    const int64_t out_row0 = static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G + hg * HPW;
+    RowSink sink;
+    sink.seq = s.seq;
+    sink.nmem = s.nmem;
+    sink.kvh = kvh;
+    sink.row0 = hg * HPW;
+    sink.side = s.grp >= 0 ? 0 : 1;
+    sink.cas = 0u;
+    if (CAS) {
+      // Members with both a shared prefix and tokens of their own: this entry is one side of
+      // their cascade, merged with the other side by whichever finishes second.
+      const bool both = lane < s.nmem && (s.grp >= 0 ? ps.lens[w.V + s.seq + lane] > 0 : ps.hp[s.seq] > 0);
+      sink.cas = __ballot_sync(0xffffffffu, both);
+    }
+    const int nh_warp = min(HPW, s.nmem * G - hg * HPW);  // this warp's rows that are not padding
+    const int nh_member = min(HPW, G - hg * HPW);         // one member's rows in this warp's group
     if (s.whole) {
+      float inv[NT][2], lse[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int hl = nt * 8 + 2 * t4 + e;
-          if (hg * HPW + hl >= G) continue;
-          const float inv = l_run[nt][e] > 0.0f ? v_scale / l_run[nt][e] : 0.0f;
-          T* orow = out + (out_row0 + hl) * D;
-#pragma unroll
-          for (int c = 0; c < NCH; ++c) {
-#pragma unroll
-            for (int h = 0; h < OW / 8; ++h) {
-              const int m0 = c * (OW / 2) + 4 * h;
-              uint4 pk;
-              pk.x = Storage<T>::pack2(acc[m0 + 0][nt][e] * inv, acc[m0 + 0][nt][e + 2] * inv);
-              pk.y = Storage<T>::pack2(acc[m0 + 1][nt][e] * inv, acc[m0 + 1][nt][e + 2] * inv);
-              pk.z = Storage<T>::pack2(acc[m0 + 2][nt][e] * inv, acc[m0 + 2][nt][e + 2] * inv);
-              pk.w = Storage<T>::pack2(acc[m0 + 3][nt][e] * inv, acc[m0 + 3][nt][e + 2] * inv);
-              *reinterpret_cast<uint4*>(orow + c * 8 * OW + OW * g + 8 * h) = pk;
-            }
-          }
+          const float l = l_run[nt][e];
+          inv[nt][e] = l > 0.0f ? v_scale / l : 0.0f;
+          lse[nt][e] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
         }
       }
+      store_rows<T, D, NT, OW, CAS>(a, sink, acc, inv, lse, g, t4, nh_warp);
+      if (CAS && sink.cas != 0u) cascade_arrive<T, D>(a, sink, hg, hg * HPW, nh_member, lane);
       continue;
     }
     // This chunk's normalised partial and base-2 LSE, in the fragment layout; padding heads of
@@ -963,7 +1264,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     // Few chunks: the last one merges from its registers (written only if it must publish).
     // Many: every chunk writes its partial and the last merges them all with the flat merge.
     const bool flat = s.nchunks > kRegisterMergeChunks;
-    uint32_t* counter = counter_of(a, s.b, kvh, hg);
+    uint32_t* counter = counter_of(a, s.cb, kvh, hg);
     const uint32_t siblings = static_cast<uint32_t>(s.nchunks - 1);
     bool last = __shfl_sync(0xffffffffu, published, 0) == siblings;
     if (flat || !last) {
@@ -973,7 +1274,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int hl = nt * 8 + 2 * t4 + e;
-          if (hg * HPW + hl >= G) continue;
+          if (hl >= nh_warp) continue;
           float* po = a.part_o + (slot * HPW + hl) * D;
 #pragma unroll
           for (int c = 0; c < NCH; ++c) {
@@ -1001,7 +1302,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     }
     __syncwarp();
     if (flat) {
-      merge_chunks<T, D, HPW>(a, s, HT * HG, mu, min(HPW, G - hg * HPW), out + out_row0 * D, lane);
+      merge_chunks<T, D, HPW, CAS>(a, s, HT * HG, mu, nh_warp, sink, lane);
     } else {
       // Merge in chunk order with a running max, this chunk's own term from its registers (the
       // values it would have stored), so the result does not depend on which chunk merges; a
@@ -1029,7 +1330,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           for (int ei = 0; ei < EG; ++ei) {
             const int e = ne % 2 + ei;
             const int hl = nt * 8 + 2 * t4 + e;
-            const bool ld = !own && hg * HPW + hl < G;
+            const bool ld = !own && hl < nh_warp;
             const float* po = a.part_o + (slot2 * HPW + hl) * D;
             lse[ei] = own ? lse_own[nt][e] : ld ? __ldcg(a.part_lse + slot2 * HPW + hl) : -INFINITY;
 #pragma unroll
@@ -1067,30 +1368,19 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           }
         }
       }
+      float inv[NT][2], lse[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int hl = nt * 8 + 2 * t4 + e;
-          if (hg * HPW + hl >= G) continue;
-          const float inv = w_acc[nt][e] > 0.0f ? 1.0f / w_acc[nt][e] : 0.0f;
-          T* orow = out + (out_row0 + hl) * D;
-#pragma unroll
-          for (int c = 0; c < NCH; ++c) {
-#pragma unroll
-            for (int h = 0; h < OW / 8; ++h) {
-              const int m0 = c * (OW / 2) + 4 * h;
-              uint4 pk;
-              pk.x = Storage<T>::pack2(o_acc[m0 + 0][nt][e] * inv, o_acc[m0 + 0][nt][e + 2] * inv);
-              pk.y = Storage<T>::pack2(o_acc[m0 + 1][nt][e] * inv, o_acc[m0 + 1][nt][e + 2] * inv);
-              pk.z = Storage<T>::pack2(o_acc[m0 + 2][nt][e] * inv, o_acc[m0 + 2][nt][e + 2] * inv);
-              pk.w = Storage<T>::pack2(o_acc[m0 + 3][nt][e] * inv, o_acc[m0 + 3][nt][e + 2] * inv);
-              *reinterpret_cast<uint4*>(orow + c * 8 * OW + OW * g + 8 * h) = pk;
-            }
-          }
+          const float wsum = w_acc[nt][e];
+          inv[nt][e] = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+          lse[nt][e] = wsum > 0.0f ? m_acc[nt][e] + __log2f(wsum) : -INFINITY;
         }
       }
+      store_rows<T, D, NT, OW, CAS>(a, sink, o_acc, inv, lse, g, t4, nh_warp);
     }
+    if (CAS && sink.cas != 0u) cascade_arrive<T, D>(a, sink, hg, hg * HPW, nh_member, lane);
     // Every sibling has counted (or none needed to): nobody else touches the counter in this
     // launch, so a plain store returns it to zero for the next one.
     if (lane == 0) *reinterpret_cast<volatile uint32_t*>(counter) = 0u;
@@ -1144,22 +1434,26 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
   float* l_s = reinterpret_cast<float*>(gsmem + L.l);
   float* al_s = reinterpret_cast<float*>(gsmem + L.alpha);
   int64_t* row_s = reinterpret_cast<int64_t*>(gsmem + L.rows);
-  int* misc = reinterpret_cast<int*>(gsmem + L.misc);
-  int* prefix = reinterpret_cast<int*>(gsmem + L.prefix);
-  int* lens = reinterpret_cast<int*>(gsmem + L.lens);
+  PlanSmem ps;
+  ps.misc = reinterpret_cast<int*>(gsmem + L.misc);
+  ps.prefix = reinterpret_cast<int*>(gsmem + L.prefix);
+  ps.lens = reinterpret_cast<int*>(gsmem + L.lens);
+  ps.hp = nullptr;  // no cascade on this kernel
+  ps.vstart = nullptr;
+  int* misc = ps.misc;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  plan_build(a, lens, prefix, misc);
-  zero_empty_sequences<T>(a, lens, tid, kGenThreads);
+  plan_build(a, ps);
+  zero_empty_sequences<T>(a, ps.lens, nullptr, tid, kGenThreads);
   const int64_t tok_stride = static_cast<int64_t>(H) * D;
   T* out = static_cast<T*>(a.out);
 
   Walk w;
   walk_init(a, misc, w);
   Seg s;
-  while (walk_next(a, lens, prefix, w, s)) {
+  while (walk_next(a, ps, w, s)) {
     const int kvh = s.u;
-    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G) * D;
+    const T* qb = static_cast<const T*>(a.q) + (static_cast<int64_t>(s.seq) * a.num_q_heads + kvh * G) * D;
     for (int i = tid; i < G * D; i += kGenThreads) {
       q_s[i] = Storage<T>::load(qb[i]);
       acc_s[i] = 0.0f;
@@ -1170,7 +1464,7 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
     }
     const T* kc = static_cast<const T*>(a.k_cache) + kvh * D;
     const T* vc = static_cast<const T*>(a.v_cache) + kvh * D;
-    const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.b) * a.bt_stride;
+    const int32_t* bt_row = a.block_table + static_cast<int64_t>(s.seq) * a.bt_stride;
     __syncthreads();
     for (int base = s.tok_begin; base < s.tok_end; base += kGenChunk) {
       const int n = min(kGenChunk, s.tok_end - base);
@@ -1233,7 +1527,7 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
       __syncthreads();
     }
 
-    const int64_t out_row0 = static_cast<int64_t>(s.b) * a.num_q_heads + kvh * G;
+    const int64_t out_row0 = static_cast<int64_t>(s.seq) * a.num_q_heads + kvh * G;
     if (s.whole) {
       for (int idx = tid; idx < G * D; idx += kGenThreads) {
         const int h = idx / D;
@@ -1253,7 +1547,7 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
     // The block barrier orders every thread's stores before thread 0's count (a release);
     // the count's acquire and the second barrier order the merge's reads after the siblings'.
     __syncthreads();
-    uint32_t* counter = counter_of(a, s.b, kvh, 0);
+    uint32_t* counter = counter_of(a, s.cb, kvh, 0);
     if (tid == 0) misc[3] = atom_add_acq_rel_gpu(counter, 1u) == static_cast<uint32_t>(s.nchunks - 1);
     __syncthreads();
     if (misc[3]) {
@@ -1300,8 +1594,21 @@ struct Plan {
   int seg_cost = 0;
   int min_tiles = kMinTilesPerCta;
   bool kv8 = false;
+  int groups = 0;   // cascade: prefix groups (0: plain decode)
+  int members = 1;  // cascade: sequences packed into one prefix item
+  size_t cas_o_off = 0, cas_lse_off = 0;  // cascade: side states within the partials buffer
   size_t part_bytes = 0, sync_bytes = 0;
   const void* fn = nullptr;
+};
+
+// Shared-prefix groups of a cascade call (groups == 0: none).
+struct CascadeIn {
+  const int32_t* bt = nullptr;
+  const int32_t* lens = nullptr;
+  const int32_t* indptr = nullptr;
+  int groups = 0;
+  int64_t bt_stride = 0;
+  int max_pages = 0;
 };
 
 std::mutex g_mu;
@@ -1339,21 +1646,20 @@ int blocks_per_sm(int dev, const void* fn, int threads, size_t smem) {
   return n;
 }
 
+template <typename T, int D, int NT, bool KV8>
+const void* tc_fn_one(bool cas) {
+  return cas ? (const void*)decode_tc_kernel<T, D, NT, KV8, true> : (const void*)decode_tc_kernel<T, D, NT, KV8, false>;
+}
+
 template <typename T>
-const void* tc_fn(int D, int NT, bool kv8) {
+const void* tc_fn(int D, int NT, bool kv8, bool cas) {
   if (kv8) {
-    if (D == 128) {
-      return NT == 1 ? (const void*)decode_tc_kernel<T, 128, 1, true> : (const void*)decode_tc_kernel<T, 128, 2, true>;
-    }
-    return (const void*)decode_tc_kernel<T, 256, 1, true>;
+    if (D == 128) return NT == 1 ? tc_fn_one<T, 128, 1, true>(cas) : tc_fn_one<T, 128, 2, true>(cas);
+    return tc_fn_one<T, 256, 1, true>(cas);
   }
-  if (D == 64) {
-    return NT == 1 ? (const void*)decode_tc_kernel<T, 64, 1, false> : (const void*)decode_tc_kernel<T, 64, 2, false>;
-  }
-  if (D == 128) {
-    return NT == 1 ? (const void*)decode_tc_kernel<T, 128, 1, false> : (const void*)decode_tc_kernel<T, 128, 2, false>;
-  }
-  return (const void*)decode_tc_kernel<T, 256, 1, false>;
+  if (D == 64) return NT == 1 ? tc_fn_one<T, 64, 1, false>(cas) : tc_fn_one<T, 64, 2, false>(cas);
+  if (D == 128) return NT == 1 ? tc_fn_one<T, 128, 1, false>(cas) : tc_fn_one<T, 128, 2, false>(cas);
+  return tc_fn_one<T, 256, 1, false>(cas);
 }
 
 const void* gen_fn(int dtype) {
@@ -1387,10 +1693,18 @@ size_t lse_offset(int slots, int slot_heads, int D) {
 
 // Launch shape and scratch sizes of one decode call. `generic` forces the CUDA-core kernel.
 // kv8: e4m3 cache (tensor-core kernel only: head_dim 128 or 256, q/out fp16 or bf16).
+// groups > 0: a cascade over that many shared-prefix groups of at most prefix_max_pages pages
+// (tensor-core kernel and balanced plan only).
 int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages, int num_splits, bool generic,
-              Plan& p, bool kv8 = false) {
+              Plan& p, bool kv8 = false, int groups = 0, int prefix_max_pages = 0) {
   if (batch <= 0 || batch > kMaxBatch || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || D <= 0 || P <= 0 ||
-      max_pages < 0 || num_splits < 0) {
+      max_pages < 0 || num_splits < 0 || groups < 0 || groups > kMaxBatch || prefix_max_pages < 0) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  const bool cascade = groups > 0;
+  if (cascade && (generic || num_splits != 0)) return static_cast<int>(cudaErrorInvalidValue);
+  // A cascade runs on the tensor-core kernel only: reject other shapes before any device query.
+  if (cascade && (dtype == KL_FLOAT32 || !(D == 64 || D == 128 || D == 256) || !(P == 8 || P % 16 == 0))) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
   if (dtype != KL_FLOAT32 && dtype != KL_FLOAT16 && dtype != KL_BFLOAT16) return static_cast<int>(cudaErrorInvalidValue);
@@ -1399,13 +1713,20 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   if (max_tokens > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
   const int64_t max_tiles = (max_tokens + kTile - 1) / kTile;
   if (static_cast<int64_t>(batch) * max_tiles * Hkv > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
+  const int64_t prefix_tokens = cascade ? static_cast<int64_t>(prefix_max_pages) * P : 0;
+  if (prefix_tokens > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
+  const int64_t prefix_tiles = (prefix_tokens + kTile - 1) / kTile;  // per prefix item (at most batch of them)
+  if (static_cast<int64_t>(batch) * prefix_tiles * Hkv > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return static_cast<int>(cudaErrorNoDevice);
   const int sms = device_sms(dev);
   if (sms <= 0) return static_cast<int>(cudaErrorNoDevice);
 
   p.D = D;
-  const int NT = (G > 8 && D <= 128) ? 2 : 1;
+  int NT = (G > 8 && D <= 128) ? 2 : 1;
+  // A cascade may widen the warps' query columns so that a prefix item packs more sequences
+  // (KL_DECODE_CASCADE_NT=2; head_dim <= 128).
+  if (cascade && env_int("KL_DECODE_CASCADE_NT") == 2 && D <= 128) NT = 2;
   const int hg_need = (G + 8 * NT - 1) / (8 * NT);
   const int HG = hg_need <= 1 ? 1 : hg_need <= 2 ? 2 : hg_need <= 4 ? 4 : 0;
   p.tc = !generic && dtype != KL_FLOAT32 && (D == (kv8 ? 128 : 64) || D == 128 || D == 256) &&
@@ -1420,7 +1741,8 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     // at most 64 KB, and enough (sequence, head-block) tiles to keep every SM busy.
     int ht = 1;
     while (ht * 2 <= 8 / HG && Hkv % (ht * 2) == 0 && ht * 2 * D <= 1024) ht *= 2;
-    while (ht > 1 && static_cast<int64_t>(batch) * max_tiles * (Hkv / ht) < 4LL * sms) ht /= 2;
+    const int64_t tiles = static_cast<int64_t>(batch) * (max_tiles + prefix_tiles);
+    while (ht > 1 && tiles * (Hkv / ht) < 4LL * sms) ht /= 2;
     const int forced_ht = env_int("KL_DECODE_HEADS_PER_TILE");
     if (forced_ht > 0 && forced_ht <= 8 / HG && Hkv % forced_ht == 0 && (forced_ht & (forced_ht - 1)) == 0 &&
         forced_ht * D <= 1024) {
@@ -1430,7 +1752,7 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     p.shape.hg = HG;
     p.shape.tw = kCW / (ht * HG);
     p.shape.p_rows = P < 16 ? P : 16;
-    const TcLayout base = tc_layout(D, NT, ht, p.shape.tw, 0, batch, eb);
+    const TcLayout base = tc_layout(D, NT, ht, p.shape.tw, 0, batch, eb, groups);
     const uint32_t stage = base.stage_bytes + 16u;
     int ns = base.total < kTcSmemBudget ? static_cast<int>((kTcSmemBudget - base.total) / stage) : 0;
     ns = std::min(kMaxStages, ns);
@@ -1443,12 +1765,15 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     ns = ns / p.shape.tw * p.shape.tw;
     if (ns < std::max(2, p.shape.tw)) return static_cast<int>(cudaErrorInvalidValue);
     p.shape.nstage = ns;
-    p.smem = tc_layout(D, NT, ht, p.shape.tw, ns, batch, eb).total;
-    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, NT, kv8) : tc_fn<__nv_bfloat16>(D, NT, kv8);
+    p.smem = tc_layout(D, NT, ht, p.shape.tw, ns, batch, eb, groups).total;
+    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, NT, kv8, cascade) : tc_fn<__nv_bfloat16>(D, NT, kv8, cascade);
     p.units = Hkv / ht;
     p.slot_heads = 8 * NT;
+    p.groups = groups;
+    p.members = HG * 8 * NT / G > 1 ? HG * 8 * NT / G : 1;
     threads = kTCThreads;
   } else {
+    if (cascade) return static_cast<int>(cudaErrorInvalidValue);
     if (static_cast<int64_t>(G) * D > 8192) return static_cast<int>(cudaErrorInvalidValue);
     p.smem = gen_layout(G, D, batch).total;
     p.fn = gen_fn(dtype);
@@ -1480,12 +1805,19 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   if (forced_min > 0) p.min_tiles = std::min(forced_min, 1 << 20);
   const int forced_cost = env_int("KL_DECODE_SEGMENT_COST");
   p.seg_cost = forced_cost < 0 ? 0 : forced_cost > 0 ? std::min(forced_cost, 64) : p.tc ? kTcSegmentCost : 0;
-  if (static_cast<int64_t>(batch) * (max_tiles + p.seg_cost) * p.units > INT_MAX / 2) {
-    return static_cast<int>(cudaErrorInvalidValue);
-  }
+  const int64_t cost = static_cast<int64_t>(batch) * (max_tiles + p.seg_cost) +
+                       (cascade ? static_cast<int64_t>(batch) * (prefix_tiles + p.seg_cost) : 0);
+  if (cost * p.units > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
   p.slots = static_cast<int>(chunks * slots_per_chunk);
   p.part_bytes = lse_offset(p.slots, p.slot_heads, D) + static_cast<size_t>(p.slots) * p.slot_heads * 4;
-  p.sync_bytes = (1 + static_cast<size_t>(batch) * Hkv * kMaxHeadGroups) * 4;
+  // Counter blocks: sequences' own tokens, then (cascade) prefix items and the per-sequence sides.
+  p.sync_bytes = (1 + static_cast<size_t>(cascade ? 3 : 1) * batch * Hkv * kMaxHeadGroups) * 4;
+  if (cascade) {
+    const size_t rows = static_cast<size_t>(batch) * Hq;
+    p.cas_o_off = (p.part_bytes + 255) / 256 * 256;
+    p.cas_lse_off = p.cas_o_off + 2 * rows * D * 4;
+    p.part_bytes = p.cas_lse_off + 2 * rows * 4;
+  }
   return 0;
 }
 
@@ -1533,23 +1865,29 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_t
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
+template <typename T, int D, int NT, bool KV8>
+cudaError_t launch_tc_one(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                          cudaStream_t st) {
+  if (p.groups > 0) {
+    decode_tc_kernel<T, D, NT, KV8, true><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+  } else {
+    decode_tc_kernel<T, D, NT, KV8, false><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+  }
+  return cudaGetLastError();
+}
+
 template <typename T, bool KV8>
 cudaError_t launch_tc_kind(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                            cudaStream_t st) {
   if constexpr (!KV8) {
     if (p.D == 64) {
-      if (p.NT == 1) decode_tc_kernel<T, 64, 1, false><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      else decode_tc_kernel<T, 64, 2, false><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-      return cudaGetLastError();
+      return p.NT == 1 ? launch_tc_one<T, 64, 1, false>(p, tmk, tmv, a, st) : launch_tc_one<T, 64, 2, false>(p, tmk, tmv, a, st);
     }
   }
   if (p.D == 128) {
-    if (p.NT == 1) decode_tc_kernel<T, 128, 1, KV8><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-    else decode_tc_kernel<T, 128, 2, KV8><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-  } else {
-    decode_tc_kernel<T, 256, 1, KV8><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
+    return p.NT == 1 ? launch_tc_one<T, 128, 1, KV8>(p, tmk, tmv, a, st) : launch_tc_one<T, 128, 2, KV8>(p, tmk, tmv, a, st);
   }
-  return cudaGetLastError();
+  return launch_tc_one<T, 256, 1, KV8>(p, tmk, tmv, a, st);
 }
 
 template <typename T>
@@ -1563,16 +1901,24 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
                 const int32_t* block_table, const int32_t* seq_lens, int batch, int Hq, int Hkv, int D, int P,
                 int64_t bt_stride, int max_pages, int64_t num_pages, float scale, int num_splits, void* partials,
                 size_t partial_bytes, void* sync, size_t sync_bytes, cudaStream_t st,
-                const float* k_scale = nullptr, const float* v_scale = nullptr) {
+                const float* k_scale = nullptr, const float* v_scale = nullptr, const CascadeIn& cas = CascadeIn{}) {
   if (batch == 0) return 0;
   if (!out || !q || !k_cache || !v_cache || !block_table || !seq_lens || !sync) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  const bool cascade = cas.groups > 0;
+  if (cascade && (!cas.bt || !cas.lens || !cas.indptr || cas.bt_stride < 0 ||
+                  (cas.groups > 1 && cas.bt_stride < cas.max_pages))) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
   const bool kv8 = k_scale != nullptr || v_scale != nullptr;
   if (kv8 && (!k_scale || !v_scale)) return static_cast<int>(cudaErrorInvalidValue);
   if (bt_stride < 0 || (batch > 1 && bt_stride < max_pages)) return static_cast<int>(cudaErrorInvalidValue);
   Plan p;
-  if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p, kv8)) return rc;
+  if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p, kv8, cas.groups,
+                               cas.max_pages)) {
+    return rc;
+  }
   // The tensor-core path needs 16-byte aligned caches (TMA), q and out (vector loads and
   // stores) and TMA row coordinates that fit in int32; otherwise take the generic kernel.
   const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 16) && aligned(out, 16) &&
@@ -1584,7 +1930,7 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
     use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8) &&
              encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8);
   }
-  if (kv8 && !use_tc) return static_cast<int>(cudaErrorInvalidValue);  // no generic e4m3 kernel
+  if ((kv8 || cascade) && !use_tc) return static_cast<int>(cudaErrorInvalidValue);  // no generic e4m3 / cascade kernel
   if (!use_tc && p.tc) {
     if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, true, p)) return rc;
   }
@@ -1618,6 +1964,17 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   a.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + lse_offset(p.slots, p.slot_heads, D));
   a.k_scale = k_scale;
   a.v_scale = v_scale;
+  a.prefix_bt = cas.bt;
+  a.prefix_lens = cas.lens;
+  a.prefix_indptr = cas.indptr;
+  a.num_prefixes = cascade ? cas.groups : 0;
+  a.prefix_bt_stride = cas.bt_stride;
+  a.prefix_max_pages = cas.max_pages;
+  a.members = p.members;
+  if (cascade) {
+    a.cas_o = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + p.cas_o_off);
+    a.cas_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + p.cas_lse_off);
+  }
 
   if (use_tc) {
     const cudaError_t e = dtype == KL_FLOAT16 ? launch_tc<__half>(p, tmk, tmv, a, st)
@@ -1687,6 +2044,48 @@ int kl_paged_decode_fp8(int dtype, void* out, const void* q, const void* k_cache
                           head_dim, page_size, block_table_stride, max_pages_per_seq, num_pages, scale, num_splits,
                           partials, partial_bytes, sync, sync_bytes, static_cast<cudaStream_t>(stream), k_scale,
                           v_scale);
+}
+
+int kl_paged_decode_cascade_workspace_size(int dtype, int batch, int num_prefixes, int num_q_heads,
+                                           int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+                                           int max_prefix_pages, size_t* partial_bytes, size_t* sync_bytes) {
+  if (!partial_bytes || !sync_bytes) return static_cast<int>(cudaErrorInvalidValue);
+  *partial_bytes = 0;
+  *sync_bytes = 4;
+  if (batch == 0) return 0;
+  if (num_prefixes == 0) {
+    return kl_paged_decode_workspace_size(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size,
+                                          max_pages_per_seq, 0, partial_bytes, sync_bytes);
+  }
+  klb::Plan p;
+  if (const int rc = klb::make_plan(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size, max_pages_per_seq,
+                                    0, false, p, false, num_prefixes, max_prefix_pages)) {
+    return rc;
+  }
+  *partial_bytes = p.part_bytes;
+  *sync_bytes = p.sync_bytes;
+  return 0;
+}
+
+int kl_paged_decode_cascade(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
+                            const float* k_scale, const float* v_scale, const int32_t* prefix_block_table,
+                            const int32_t* prefix_lens, const int32_t* prefix_indptr, int num_prefixes,
+                            int64_t prefix_block_table_stride, int max_prefix_pages, const int32_t* block_table,
+                            const int32_t* seq_lens, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                            int page_size, int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
+                            float scale, void* partials, size_t partial_bytes, void* sync, size_t sync_bytes,
+                            void* stream) {
+  if (num_prefixes < 0 || ((k_scale == nullptr) != (v_scale == nullptr))) return static_cast<int>(cudaErrorInvalidValue);
+  klb::CascadeIn cas;
+  cas.bt = prefix_block_table;
+  cas.lens = prefix_lens;
+  cas.indptr = prefix_indptr;
+  cas.groups = num_prefixes;
+  cas.bt_stride = prefix_block_table_stride;
+  cas.max_pages = max_prefix_pages;
+  return klb::decode_impl(dtype, out, q, k_cache, v_cache, block_table, seq_lens, batch, num_q_heads, num_kv_heads,
+                          head_dim, page_size, block_table_stride, max_pages_per_seq, num_pages, scale, 0, partials,
+                          partial_bytes, sync, sync_bytes, static_cast<cudaStream_t>(stream), k_scale, v_scale, cas);
 }
 
 int kl_paged_decode_attention(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,

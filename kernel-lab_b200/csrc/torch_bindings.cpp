@@ -309,6 +309,78 @@ void paged_kv_append_fp8(at::Tensor& k_cache, at::Tensor& v_cache, const at::Ten
                "paged_kv_append_fp8");
 }
 
+// Cascade (shared-prefix) decode (kl_paged_decode_cascade): the sequences of group p,
+// [prefix_indptr[p], prefix_indptr[p+1]), attend to the prefix_lens[p] tokens in the pages of
+// prefix_block_table row p and then to their own. The caches are q's dtype, or e4m3 with
+// per-KV-head scales when k_scale / v_scale are given.
+void paged_decode_attention_cascade(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                                    const at::Tensor& v_cache, const at::Tensor& prefix_block_table,
+                                    const at::Tensor& prefix_lens, const at::Tensor& prefix_indptr,
+                                    const at::Tensor& block_table, const at::Tensor& seq_lens, double scale,
+                                    const std::optional<at::Tensor>& k_scale, const std::optional<at::Tensor>& v_scale) {
+  TORCH_CHECK(q.is_cuda() && k_cache.is_cuda() && v_cache.is_cuda(), "tensors must be on CUDA");
+  TORCH_CHECK(q.dim() == 3 && k_cache.dim() == 4, "q is [batch, heads, dim]; caches are 4-D");
+  TORCH_CHECK(q.is_contiguous() && out.is_contiguous() && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "q, out and both caches must be contiguous");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes() && k_cache.scalar_type() == v_cache.scalar_type(),
+              "k_cache and v_cache differ in shape or dtype");
+  TORCH_CHECK(k_scale.has_value() == v_scale.has_value(), "give both k_scale and v_scale, or neither");
+  const bool fp8 = k_scale.has_value();
+  if (fp8) {
+    TORCH_CHECK(is_e4m3(k_cache), "with scales the caches must be float8_e4m3fn (or uint8 e4m3 codes)");
+    TORCH_CHECK(q.scalar_type() == at::kHalf || q.scalar_type() == at::kBFloat16, "q is fp16 or bf16");
+  } else {
+    TORCH_CHECK(q.scalar_type() == k_cache.scalar_type(), "q and caches must share a dtype");
+  }
+  TORCH_CHECK(out.scalar_type() == q.scalar_type() && out.sizes() == q.sizes(), "out must match q");
+  for (const at::Tensor* t : {&prefix_block_table, &prefix_lens, &prefix_indptr, &block_table, &seq_lens}) {
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->device() == q.device(),
+                "block tables, lengths and prefix_indptr must be int32 on q's device");
+  }
+  TORCH_CHECK(block_table.dim() == 2 && block_table.stride(-1) == 1 && prefix_block_table.dim() == 2 &&
+                  prefix_block_table.stride(-1) == 1 && seq_lens.is_contiguous() && prefix_lens.is_contiguous() &&
+                  prefix_indptr.is_contiguous(),
+              "block-table rows, lengths and prefix_indptr must be contiguous");
+  TORCH_CHECK(k_cache.device() == q.device() && v_cache.device() == q.device() && out.device() == q.device(),
+              "tensors must be on one device");
+  const int batch = static_cast<int>(q.size(0));
+  const int num_q_heads = static_cast<int>(q.size(1));
+  const int head_dim = static_cast<int>(q.size(2));
+  const int page_size = static_cast<int>(k_cache.size(1));
+  const int num_kv_heads = static_cast<int>(k_cache.size(2));
+  TORCH_CHECK(k_cache.size(3) == head_dim, "cache head_dim differs from q");
+  TORCH_CHECK(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "num_q_heads must be a multiple of num_kv_heads");
+  TORCH_CHECK(seq_lens.numel() == batch && block_table.size(0) == batch,
+              "block_table and seq_lens need one row / entry per sequence");
+  const int64_t groups = prefix_lens.numel();
+  TORCH_CHECK(prefix_block_table.size(0) == groups && prefix_indptr.numel() == groups + 1,
+              "prefix_block_table needs one row and prefix_indptr groups + 1 entries per prefix group");
+  if (fp8) check_scales(*k_scale, *v_scale, num_kv_heads, q.device());
+  if (batch == 0) return;
+  const int dtype = to_dtype(q.scalar_type());
+  const int max_pages = static_cast<int>(block_table.size(1));
+  const int max_prefix_pages = static_cast<int>(prefix_block_table.size(1));
+  const c10::cuda::CUDAGuard guard(q.device());
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  size_t partial_bytes = 0, sync_bytes = 0;
+  check_status(kl_paged_decode_cascade_workspace_size(dtype, batch, static_cast<int>(groups), num_q_heads,
+                                                      num_kv_heads, head_dim, page_size, max_pages, max_prefix_pages,
+                                                      &partial_bytes, &sync_bytes),
+               "paged_decode_attention_cascade (workspace)");
+  Scratch& s = scratch_for(q.device(), stream, partial_bytes, sync_bytes);
+  check_status(
+      kl_paged_decode_cascade(dtype, out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                              fp8 ? k_scale->data_ptr<float>() : nullptr, fp8 ? v_scale->data_ptr<float>() : nullptr,
+                              prefix_block_table.data_ptr<int32_t>(), prefix_lens.data_ptr<int32_t>(),
+                              prefix_indptr.data_ptr<int32_t>(), static_cast<int>(groups), prefix_block_table.stride(0),
+                              max_prefix_pages, block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), batch,
+                              num_q_heads, num_kv_heads, head_dim, page_size, block_table.stride(0), max_pages,
+                              k_cache.size(0), static_cast<float>(scale), s.partials.data_ptr(),
+                              static_cast<size_t>(s.partials.numel()), s.sync.data_ptr(),
+                              static_cast<size_t>(s.sync.numel()), stream),
+      "paged_decode_attention_cascade");
+}
+
 // Status bits (KL_STATUS_*) left by decode calls on the current device and stream.
 int64_t decode_status(bool clear) {
   const at::Device dev(at::kCUDA, c10::cuda::current_device());
@@ -337,6 +409,9 @@ void noop_decode_fp8(at::Tensor&, const at::Tensor&, const at::Tensor&, const at
                      const at::Tensor&, const at::Tensor&, const at::Tensor&, double) {}
 void noop_append_fp8(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                      const at::Tensor&, const at::Tensor&, const at::Tensor&) {}
+void noop_cascade(at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                  const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, double,
+                  const std::optional<at::Tensor>&, const std::optional<at::Tensor>&) {}
 
 }  // namespace
 
@@ -358,6 +433,10 @@ TORCH_LIBRARY(kernel_lab, m) {
   m.def(
       "paged_kv_append_fp8(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, Tensor k_scale, "
       "Tensor v_scale, Tensor block_table, Tensor positions) -> ()");
+  m.def(
+      "paged_decode_attention_cascade(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, "
+      "Tensor prefix_block_table, Tensor prefix_lens, Tensor prefix_indptr, Tensor block_table, "
+      "Tensor seq_lens, float scale, Tensor? k_scale=None, Tensor? v_scale=None) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(kernel_lab, CUDA, m) {
@@ -368,6 +447,7 @@ TORCH_LIBRARY_IMPL(kernel_lab, CUDA, m) {
   m.impl("paged_kv_append", &paged_kv_append);
   m.impl("paged_decode_attention_fp8", &paged_decode_attention_fp8);
   m.impl("paged_kv_append_fp8", &paged_kv_append_fp8);
+  m.impl("paged_decode_attention_cascade", &paged_decode_attention_cascade);
 }
 
 TORCH_LIBRARY_IMPL(kernel_lab, Meta, m) {
@@ -378,6 +458,7 @@ TORCH_LIBRARY_IMPL(kernel_lab, Meta, m) {
   m.impl("paged_kv_append", &noop_append);
   m.impl("paged_decode_attention_fp8", &noop_decode_fp8);
   m.impl("paged_kv_append_fp8", &noop_append_fp8);
+  m.impl("paged_decode_attention_cascade", &noop_cascade);
 }
 
 // Importing kernel_lab._C runs the registrations above.

@@ -59,6 +59,15 @@ SIGNATURES = {
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_i64,
          _c_int, _c_i64, _c_i64, _c_vp, _c_vp],
     ),
+    "kl_paged_decode_cascade_workspace_size": (
+        _c_int,
+        [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_szp, _c_szp],
+    ),
+    "kl_paged_decode_cascade": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_i64, _c_int, _c_vp, _c_vp,
+         _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int, _c_i64, _c_float, _c_vp, _c_sz, _c_vp, _c_sz, _c_vp],
+    ),
     "kl_paged_decode_noalloc": (
         _c_int,
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int,
@@ -303,3 +312,51 @@ def paged_kv_append_fp8(
         ),
         "kl_paged_kv_append_fp8",
     )
+
+
+def paged_decode_cascade(
+    out: torch.Tensor,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    prefix_block_table: torch.Tensor,
+    prefix_lens: torch.Tensor,
+    prefix_indptr: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    k_scale: torch.Tensor | None = None,
+    v_scale: torch.Tensor | None = None,
+    scratch: DecodeScratch | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> DecodeScratch:
+    """kl_paged_decode_cascade on torch tensors (e4m3 caches when k_scale / v_scale are given);
+    returns the scratch used."""
+    batch, hq, d = q.shape
+    num_pages, page, hkv, _ = k_cache.shape
+    groups = prefix_lens.numel()
+    if scratch is None:
+        pb, sb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        _check(
+            load().kl_paged_decode_cascade_workspace_size(
+                DTYPE_CODES[q.dtype], batch, groups, hq, hkv, d, page, block_table.shape[1],
+                prefix_block_table.shape[1], ctypes.byref(pb), ctypes.byref(sb),
+            ),
+            "kl_paged_decode_cascade_workspace_size",
+        )
+        scratch = DecodeScratch(
+            partials=torch.empty(max(pb.value, 256), dtype=torch.uint8, device=q.device),
+            sync=torch.zeros(max(sb.value, 256), dtype=torch.uint8, device=q.device),
+        )
+    scale = d**-0.5 if scale is None else scale
+    _check(
+        load().kl_paged_decode_cascade(
+            DTYPE_CODES[q.dtype], _ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k_scale), _ptr(v_scale),
+            _ptr(prefix_block_table), _ptr(prefix_lens), _ptr(prefix_indptr), groups, prefix_block_table.stride(0),
+            prefix_block_table.shape[1], _ptr(block_table), _ptr(seq_lens), batch, hq, hkv, d, page,
+            block_table.stride(0), block_table.shape[1], num_pages, scale, _ptr(scratch.partials),
+            scratch.partials.numel(), _ptr(scratch.sync), scratch.sync.numel(), _stream(stream),
+        ),
+        "kl_paged_decode_cascade",
+    )
+    return scratch

@@ -129,6 +129,33 @@ def paged_kv_append_fp8(
     torch.ops.kernel_lab.paged_kv_append_fp8(k_cache, v_cache, k_new, v_new, k_scale, v_scale, block_table, positions)
 
 
+def paged_decode_attention_cascade(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    prefix_block_table: torch.Tensor,
+    prefix_lens: torch.Tensor,
+    prefix_indptr: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    k_scale: torch.Tensor | None = None,
+    v_scale: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Shared-prefix (cascade) decode: the sequences of group p, ``prefix_indptr[p]`` up to
+    ``prefix_indptr[p + 1]``, attend to the ``prefix_lens[p]`` tokens held in the pages of row p
+    of ``prefix_block_table`` and then to their own ``seq_lens[b]`` tokens (``block_table`` row b).
+    A prefix's pages are read once per block of its group's sequences, not once per sequence.
+    With ``k_scale`` / ``v_scale`` the caches are e4m3 (torch.float8_e4m3fn)."""
+    _require()
+    out = torch.empty_like(q)
+    torch.ops.kernel_lab.paged_decode_attention_cascade(
+        out, q, k_cache, v_cache, prefix_block_table, prefix_lens, prefix_indptr, block_table, seq_lens,
+        q.shape[-1] ** -0.5 if scale is None else scale, k_scale, v_scale,
+    )
+    return out
+
+
 def decode_status(clear: bool = False) -> int:
     """KL_STATUS_* bits left by decode and append calls on the current device and stream
     (synchronises)."""

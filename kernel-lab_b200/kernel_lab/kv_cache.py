@@ -200,6 +200,87 @@ def random_paged_pool(
     return q, PagedKV(k_cache=k_cache, v_cache=v_cache, block_table=table, seq_lens=seq, page_size=page_size)
 
 
+@dataclass
+class CascadeKV:
+    """A paged pool holding shared prefixes and per-sequence tokens, with the cascade tables:
+    group p = sequences prefix_indptr[p] .. prefix_indptr[p+1]-1, sharing prefix_lens[p] tokens
+    in the pages of prefix_block_table row p; sequence b's own tokens in block_table row b."""
+
+    k_cache: torch.Tensor
+    v_cache: torch.Tensor
+    prefix_block_table: torch.Tensor
+    prefix_lens: torch.Tensor
+    prefix_indptr: torch.Tensor
+    block_table: torch.Tensor
+    seq_lens: torch.Tensor
+    page_size: int
+
+    def concatenated_tables(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """(block_table, seq_lens) of the same problem without sharing: each sequence's row
+        lists its group's prefix pages, then its own. Exact only when every prefix length is a
+        multiple of the page size (a partial prefix page would sit in the middle)."""
+        indptr = self.prefix_indptr.tolist()
+        plens = self.prefix_lens.tolist()
+        group = [p for p in range(len(plens)) for _ in range(indptr[p], indptr[p + 1])]
+        rows, lens = [], []
+        for b, n in enumerate(self.seq_lens.tolist()):
+            pl = plens[group[b]]
+            pp = pages_for(pl, self.page_size)
+            rows.append(self.prefix_block_table[group[b], :pp].tolist() +
+                        self.block_table[b, : pages_for(n, self.page_size)].tolist())
+            lens.append(pl + n)
+        width = max(1, max(len(r) for r in rows))
+        table = torch.zeros((len(rows), width), dtype=torch.int32)
+        for b, r in enumerate(rows):
+            table[b, : len(r)] = torch.tensor(r, dtype=torch.int32)
+        dev = self.block_table.device
+        return table.to(dev), torch.tensor(lens, dtype=torch.int32, device=dev)
+
+
+def random_cascade_problem(
+    group_sizes: list[int],
+    prefix_lens: list[int],
+    seq_lens: list[int],
+    num_q_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    page_size: int,
+    dtype: torch.dtype = torch.bfloat16,
+    device: str | torch.device = "cuda",
+    seed: int = 0,
+    poison: float = NAN,
+) -> tuple[torch.Tensor, CascadeKV]:
+    """A seeded shared-prefix problem: len(group_sizes) groups of consecutive sequences (sizes
+    summing to len(seq_lens)), group p's prefix of prefix_lens[p] tokens, and each sequence's
+    own seq_lens[b] tokens, all in one shuffled pool with poisoned spare pages
+    (random_paged_pool over the prefixes followed by the sequences)."""
+    assert len(group_sizes) == len(prefix_lens) and sum(group_sizes) == len(seq_lens)
+    groups = len(prefix_lens)
+    q_all, kv = random_paged_pool(
+        [*prefix_lens, *seq_lens], num_q_heads, num_kv_heads, head_dim, page_size, dtype=dtype, device=device,
+        seed=seed, poison=poison,
+    )
+    dev = kv.block_table.device
+    table = kv.block_table
+    wp = max(1, max(pages_for(n, page_size) for n in prefix_lens))
+    ws = max(1, max(pages_for(n, page_size) for n in seq_lens))
+    if table.shape[1] < max(wp, ws):
+        table = torch.nn.functional.pad(table, (0, max(wp, ws) - table.shape[1]))
+    indptr = [0]
+    for g in group_sizes:
+        indptr.append(indptr[-1] + g)
+    return q_all[groups:].contiguous(), CascadeKV(
+        k_cache=kv.k_cache,
+        v_cache=kv.v_cache,
+        prefix_block_table=table[:groups, :wp].contiguous(),
+        prefix_lens=torch.tensor(prefix_lens, dtype=torch.int32, device=dev),
+        prefix_indptr=torch.tensor(indptr, dtype=torch.int32, device=dev),
+        block_table=table[groups:, :ws].contiguous(),
+        seq_lens=torch.tensor(seq_lens, dtype=torch.int32, device=dev),
+        page_size=page_size,
+    )
+
+
 def quantize_e4m3(cache: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     """A [num_pages, page, num_kv_heads, head_dim] cache as e4m3 codes with per-KV-head scales:
     e4m3(x / scale[h]), rounded to nearest-even and saturated to +-448 (NaN poison stays NaN),

@@ -122,7 +122,71 @@ def paged_decode_attention(
     return round_to(out, dtype)
 
 
+def _gather_tokens(cache: np.ndarray, pages_row: np.ndarray, length: int) -> np.ndarray:
+    """First ``length`` token rows [L, Hkv, D] of the pages listed in ``pages_row``."""
+    page_size = cache.shape[1]
+    pages = np.asarray(pages_row[: (length + page_size - 1) // page_size], dtype=np.int64)
+    return np.asarray(cache[pages], np.float32).reshape(-1, cache.shape[2], cache.shape[3])[:length]
+
+
+def paged_decode_attention_cascade(
+    q: np.ndarray,
+    k_cache: np.ndarray,
+    v_cache: np.ndarray,
+    prefix_block_table: np.ndarray,
+    prefix_lens: np.ndarray,
+    prefix_indptr: np.ndarray,
+    block_table: np.ndarray,
+    seq_lens: np.ndarray,
+    scale: float | None = None,
+    dtype: str = "f32",
+) -> np.ndarray:
+    """Shared-prefix (cascade) decode: sequence b of group p (prefix_indptr[p] <= b <
+    prefix_indptr[p+1]) attends to the prefix_lens[p] tokens of row p of prefix_block_table
+    followed by its own seq_lens[b] tokens (row b of block_table). kernel-lab has no cascade
+    (its design notes name it as FlashInfer's addition, docs/design.md:96-102); the result is
+    kernel-lab's reference decode math (kernel_lab/reference.py:33-68) over that concatenated
+    token list. A group table that does not partition the batch (first entry 0, non-decreasing,
+    last entry batch) makes the prefixes ignored, as the kernel does.
+    """
+    q = np.asarray(q, dtype=np.float32)
+    batch, num_q_heads, head_dim = q.shape
+    num_kv_heads = k_cache.shape[2]
+    group = num_q_heads // num_kv_heads
+    scale = head_dim**-0.5 if scale is None else scale
+    indptr = np.asarray(prefix_indptr, dtype=np.int64)
+    groups = len(prefix_lens)
+    valid = groups > 0 and indptr[0] == 0 and indptr[groups] == batch and bool(np.all(np.diff(indptr) >= 0))
+    prefix_cap = prefix_block_table.shape[1] * k_cache.shape[1]
+    own_cap = block_table.shape[1] * k_cache.shape[1]
+    out = np.zeros_like(q)
+    for b in range(batch):
+        ks, vs = [], []
+        if valid:
+            p = int(np.searchsorted(indptr, b, side="right")) - 1
+            plen = min(max(int(prefix_lens[p]), 0), prefix_cap)
+            if plen > 0:
+                ks.append(_gather_tokens(k_cache, prefix_block_table[p], plen))
+                vs.append(_gather_tokens(v_cache, prefix_block_table[p], plen))
+        length = min(max(int(seq_lens[b]), 0), own_cap)
+        if length > 0:
+            ks.append(_gather_tokens(k_cache, block_table[b], length))
+            vs.append(_gather_tokens(v_cache, block_table[b], length))
+        if not ks:
+            continue
+        k = np.ascontiguousarray(np.concatenate(ks).transpose(1, 0, 2))
+        v = np.ascontiguousarray(np.concatenate(vs).transpose(1, 0, 2))
+        qb = q[b].reshape(num_kv_heads, group, head_dim)
+        scores = np.matmul(qb, k.transpose(0, 2, 1)) * np.float32(scale)
+        scores -= scores.max(axis=-1, keepdims=True)
+        probs = np.exp(scores, dtype=np.float32)
+        probs /= probs.sum(axis=-1, keepdims=True, dtype=np.float32)
+        out[b] = np.matmul(probs, v).reshape(num_q_heads, head_dim)
+    return round_to(out, dtype)
+
+
 KL_STATUS_BAD_PAGE = 1
+KL_STATUS_BAD_PREFIX_GROUPS = 8
 
 # ---------------------------------------------------------------- e4m3 (float8 "fn": no infinities)
 #

@@ -40,6 +40,8 @@ def test_header_declares_the_abi():
         "kl_paged_kv_append",
         "kl_paged_decode_fp8",
         "kl_paged_kv_append_fp8",
+        "kl_paged_decode_cascade_workspace_size",
+        "kl_paged_decode_cascade",
     ]
 
 
@@ -87,6 +89,17 @@ def test_noop_and_validation_without_a_device():
     assert lib.kl_paged_kv_append(2, *([1] * 6), 4, 8, 128, 16, 4, 4, 10, 1000, None, None) == (
         CUDA_ERROR_INVALID_VALUE
     )
+    # Cascade: batch 0 is a no-op; missing prefix tables, forced shapes off the tensor-core path
+    # (fp32) and a prefix table narrower than its width are rejected before any launch.
+    cas = lambda dt, batch, groups, ptr, d=128, pstride=4: lib.kl_paged_decode_cascade(  # noqa: E731
+        dt, *([1] * 4), None, None, ptr, ptr, ptr, groups, pstride, 4, *([1] * 2), batch, 32, 8, d, 16, 4, 4, 10,
+        0.1, 1, 1 << 20, 1, 1 << 20, None)
+    assert cas(2, 0, 1, 1) == 0
+    assert cas(2, 4, 1, None) == CUDA_ERROR_INVALID_VALUE
+    assert cas(0, 4, 1, 1) == CUDA_ERROR_INVALID_VALUE
+    assert cas(2, 4, 2, 1, pstride=3) == CUDA_ERROR_INVALID_VALUE
+    assert lib.kl_paged_decode_cascade_workspace_size(2, 0, 1, 32, 8, 128, 16, 4, 4, ctypes.byref(size),
+                                                      ctypes.byref(size)) == 0
 
 
 # kernel-lab's schema strings, verbatim (csrc/torch_bindings.cpp:108-113 there).
@@ -107,8 +120,9 @@ def test_torch_ops_have_the_reference_schemas():
         op = getattr(torch.ops.kernel_lab, name)
         assert str(op.default._schema) == str(torch._C.parse_schema("kernel_lab::" + schema))
     assert "num_splits" in str(torch.ops.kernel_lab.paged_decode_attention_splits.default._schema)
-    for name in ("paged_decode_attention_fp8", "paged_kv_append_fp8"):
+    for name in ("paged_decode_attention_fp8", "paged_kv_append_fp8", "paged_decode_attention_cascade"):
         assert "k_scale" in str(getattr(torch.ops.kernel_lab, name).default._schema)
+    assert "prefix_indptr" in str(torch.ops.kernel_lab.paged_decode_attention_cascade.default._schema)
     assert str(torch.ops.kernel_lab.paged_kv_append.default._schema) == str(torch._C.parse_schema(
         "kernel_lab::paged_kv_append(Tensor! k_cache, Tensor! v_cache, Tensor k_new, Tensor v_new, "
         "Tensor block_table, Tensor positions) -> ()"))
@@ -130,6 +144,9 @@ def test_meta_kernels_trace_without_a_device():
     torch.ops.kernel_lab.paged_decode_attention(torch.empty_like(q), q, kc, kc, bt, ln, 0.125)
     kn = torch.empty(2, 2, 64, device="meta", dtype=torch.bfloat16)
     torch.ops.kernel_lab.paged_kv_append(kc, torch.empty_like(kc), kn, kn, bt, ln)
+    pi = torch.empty(2, device="meta", dtype=torch.int32)
+    torch.ops.kernel_lab.paged_decode_attention_cascade(torch.empty_like(q), q, kc, kc, bt, ln, pi[:1].expand(1),
+                                                        bt, ln, 0.125)
 
 
 def test_cuda_ops_fail_loudly_without_a_device():

@@ -23,6 +23,8 @@ from __future__ import annotations
 import ctypes
 import json
 
+import numpy as np
+
 import pytest
 import torch
 import torch.nn.functional as F
@@ -237,3 +239,74 @@ def test_fused_add_rms_norm_against_kernel_lab_on_the_same_gpu(rows, hidden):
     _report(f"rmsnorm_fused_{rows}x{hidden}_bf16", rms_norm_work(rows, hidden, 2, True).bytes, times)
     if rows >= 4096:
         assert times["b200"] < times["kernel_lab_cuda"]
+
+
+def flashinfer_cascade(q, kv):
+    """FlashInfer's two-level cascade (shared-prefix prefill per group + per-sequence decode,
+    merged by LSE), or None when its API does not run on this box."""
+    try:
+        import flashinfer
+
+        b, hq, d = q.shape
+        _, page, hkv, _ = kv.k_cache.shape
+        dev = q.device
+
+        def level(rows, lens):
+            npages = [-(-int(n) // page) for n in lens]
+            indptr = torch.tensor([0, *np.cumsum(npages).tolist()], dtype=torch.int32, device=dev)
+            indices = torch.cat([rows[i, :n] for i, n in enumerate(npages)]).contiguous()
+            last = torch.tensor([int(n) - (p - 1) * page for n, p in zip(lens, npages)], dtype=torch.int32, device=dev)
+            return indptr, indices, last
+
+        p_indptr, p_idx, p_last = level(kv.prefix_block_table, kv.prefix_lens.tolist())
+        s_indptr, s_idx, s_last = level(kv.block_table, kv.seq_lens.tolist())
+        ws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        wrapper = flashinfer.MultiLevelCascadeAttentionWrapper(2, ws, "NHD")
+        wrapper.plan([kv.prefix_indptr, torch.arange(b + 1, dtype=torch.int32, device=dev)], [p_indptr, s_indptr],
+                     [p_idx, s_idx], [p_last, s_last], hq, hkv, d, page, q_data_type=q.dtype, kv_data_type=q.dtype)
+        out = wrapper.run(q, (kv.k_cache, kv.v_cache))
+        return lambda: wrapper.run(q, (kv.k_cache, kv.v_cache)), out
+    except Exception as exc:  # a comparator that does not run is reported, not failed
+        print(f"COMPARATOR flashinfer cascade unavailable: {type(exc).__name__}: {exc}")
+        return None
+
+
+CASCADE_CONFIGS = [
+    # (name, group sizes, prefix lens, own lens) with Llama-3-8B heads (32/8/128), page 16, bf16
+    ("cascade_b64_prefix4096_own512", [64], [4096], [512] * 64),
+    ("cascade_8x8_prefix2048_own256", [8] * 8, [2048] * 8, [256] * 64),
+]
+
+
+@pytest.mark.parametrize("name,groups,plens,lens", CASCADE_CONFIGS)
+def test_cascade_against_flashinfer_on_the_same_gpu(name, groups, plens, lens):
+    """Shared-prefix decode: this repository's one-launch cascade, the same problem without
+    sharing through its plain decode, FlashInfer's two-level cascade and FlashInfer's plain decode.
+    Bytes are the unique KV bytes (each prefix once) plus q and out."""
+    from kernel_lab import cuda_ops
+    from kernel_lab.kv_cache import random_cascade_problem
+
+    q, kv = random_cascade_problem(groups, plens, lens, 32, 8, 128, 16, dtype=torch.bfloat16, device="cuda", seed=5)
+    table, clens = kv.concatenated_tables()
+    args = (kv.k_cache, kv.v_cache, kv.prefix_block_table, kv.prefix_lens, kv.prefix_indptr, kv.block_table,
+            kv.seq_lens)
+    ours = cuda_ops.paged_decode_attention_cascade(q, *args)
+    unique = (sum(plens) + sum(lens)) * 8 * 128 * 2 * 2 + 2 * len(lens) * 32 * 128 * 2
+    times = {
+        "b200_cascade": device_us(lambda: cuda_ops.paged_decode_attention_cascade(q, *args), 50),
+        "b200_plain_concat": device_us(
+            lambda: cuda_ops.paged_decode_attention(q, kv.k_cache, kv.v_cache, table, clens), 50),
+    }
+    fi = flashinfer_cascade(q, kv)
+    if fi is not None:
+        run, fi_out = fi
+        torch.cuda.synchronize()
+        torch.testing.assert_close(fi_out, ours, **tolerance(torch.bfloat16))
+        times["flashinfer_cascade"] = device_us(run, 30)
+    ctx = max(clens.tolist())
+    if all(n == ctx for n in clens.tolist()):
+        plain = type("KV", (), {"k_cache": kv.k_cache, "v_cache": kv.v_cache, "block_table": table})()
+        fi2 = flashinfer_decode(q, plain, ctx)
+        if fi2 is not None:
+            times["flashinfer_plain_concat"] = device_us(fi2[0], 30)
+    _report(name, unique, times)

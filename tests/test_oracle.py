@@ -207,3 +207,84 @@ def test_fp8_append_oracle_quantises_then_scatters():
     np.testing.assert_allclose(got[0], k_new[0, 0], rtol=2**-3)
     assert oracle.e4m3_decode(k2[0, 1, 1])[3] == 448.0
     assert (k2[1:] == 0).all() and (k2[0, 0] == 0).all()
+
+
+# ---------------------------------------------------------------- cascade (shared prefix)
+#
+# kernel-lab has no cascade, so the cascade oracle is pinned to the pinned decode oracle: with
+# page-aligned prefixes it must equal plain decode over the concatenated block tables bit for bit,
+# and with ragged prefixes it must equal a per-token loop written independently of both.
+
+
+def _cascade_case(group_sizes, prefix_lens, seq_lens, hq=8, hkv=2, d=32, page=8, seed=3):
+    from kernel_lab.kv_cache import random_cascade_problem
+
+    q, kv = random_cascade_problem(
+        group_sizes, prefix_lens, seq_lens, hq, hkv, d, page, dtype=torch.float32, device="cpu", seed=seed
+    )
+    return q.numpy(), kv
+
+
+def _np(kv, name):
+    return getattr(kv, name).numpy()
+
+
+def _oracle_cascade(q, kv, **kw):
+    return oracle.paged_decode_attention_cascade(
+        q, _np(kv, "k_cache"), _np(kv, "v_cache"), _np(kv, "prefix_block_table"), _np(kv, "prefix_lens"),
+        _np(kv, "prefix_indptr"), _np(kv, "block_table"), _np(kv, "seq_lens"), **kw
+    )
+
+
+def test_cascade_oracle_equals_plain_decode_over_concatenated_tables():
+    q, kv = _cascade_case([3, 1, 0, 4], [16, 0, 24, 40], [5, 0, 9, 17, 1, 8, 0, 30])
+    table, lens = kv.concatenated_tables()
+    want = oracle.paged_decode_attention(q, _np(kv, "k_cache"), _np(kv, "v_cache"), table.numpy(), lens.numpy())
+    got = _oracle_cascade(q, kv)
+    assert np.array_equal(got, want)
+
+
+def test_cascade_oracle_ragged_prefix_matches_token_loop():
+    q, kv = _cascade_case([2, 3], [13, 7], [3, 0, 11, 6, 2], seed=5)
+    k_cache, v_cache = _np(kv, "k_cache"), _np(kv, "v_cache")
+    page = kv.page_size
+    indptr = kv.prefix_indptr.tolist()
+    hq, d = q.shape[1], q.shape[2]
+    g = hq // k_cache.shape[2]
+    want = np.zeros_like(q)
+    for p in range(len(indptr) - 1):
+        for b in range(indptr[p], indptr[p + 1]):
+            rows = [(int(kv.prefix_block_table[p, t // page]), t % page) for t in range(int(kv.prefix_lens[p]))]
+            rows += [(int(kv.block_table[b, t // page]), t % page) for t in range(int(kv.seq_lens[b]))]
+            for h in range(hq):
+                if not rows:
+                    continue
+                s = np.array([float(np.dot(q[b, h], k_cache[pg, sl, h // g])) for pg, sl in rows]) * d**-0.5
+                w = np.exp(s - s.max())
+                w /= w.sum()
+                want[b, h] = sum(wi * v_cache[pg, sl, h // g] for wi, (pg, sl) in zip(w, rows))
+    got = _oracle_cascade(q, kv)
+    np.testing.assert_allclose(got, want, atol=2e-6, rtol=1e-5)
+
+
+def test_cascade_oracle_ignores_prefixes_when_groups_do_not_partition_the_batch():
+    q, kv = _cascade_case([2, 2], [16, 8], [4, 5, 6, 7])
+    kv.prefix_indptr = torch.tensor([0, 3, 2], dtype=torch.int32)  # decreasing
+    got = _oracle_cascade(q, kv)
+    want = oracle.paged_decode_attention(q, _np(kv, "k_cache"), _np(kv, "v_cache"), _np(kv, "block_table"),
+                                         _np(kv, "seq_lens"))
+    assert np.array_equal(got, want)
+
+
+def test_cascade_builder_tables_are_disjoint_and_spares_poisoned():
+    _, kv = _cascade_case([2, 1], [17, 9], [4, 0, 23])
+    page = kv.page_size
+    used = set()
+    for p, n in enumerate(kv.prefix_lens.tolist()):
+        used |= set(kv.prefix_block_table[p, : -(-n // page)].tolist())
+    for b, n in enumerate(kv.seq_lens.tolist()):
+        row = set(kv.block_table[b, : -(-n // page)].tolist())
+        assert not (row & used)
+        used |= row
+    spare = sorted(set(range(kv.k_cache.shape[0])) - used)
+    assert spare and torch.isnan(kv.k_cache[spare]).all() and torch.isnan(kv.v_cache[spare]).all()
