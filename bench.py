@@ -43,6 +43,8 @@ sys.path[:0] = [str(REPO), str(REPO / "kernel-lab_b200")]
 METRIC = "paged decode attn % of B200 peak HBM BW (Llama-3-8B GQA bs64 ctx4096); us/call"
 RMS_METRIC = "fused add+RMSNorm % of B200 peak HBM BW (4096 tokens x 8192 hidden, bf16); us/call"
 FP8_METRIC = "paged decode attn, e4m3 KV cache, algorithmic HBM GB/s (Llama-3-8B GQA bs64 ctx4096); us/call"
+CASCADE_METRIC = ("cascade (shared-prefix) decode, unique KV bytes GB/s (Llama-3-8B GQA, 64 sequences sharing a "
+                  "4096-token prefix + 512 own tokens each); us/call")
 L2_NOTE = "inputs larger than L2 (no flush needed)"
 
 
@@ -52,7 +54,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "ours", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["decode", "decode_fp8", "decode70b", "rmsnorm"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "decode_fp8", "decode70b", "cascade", "rmsnorm"], default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, help="override the workload's batch (per GPU for weak scaling)")
@@ -72,6 +74,12 @@ def workload_spec(name: str, world: int) -> dict:
                     layout="sequences", kv8=True,
                     desc="paged decode, e4m3 KV cache, Llama-3-8B heads 32/8/128, page 16, bf16 q/out, "
                          "batch 64/GPU, ctx 4096")
+    if name == "cascade":
+        # Shared prefix: each GPU's 64 sequences share one 4096-token prefix and own 512 tokens.
+        return dict(kind="decode", batch=64 * world, ctx=512, prefix=4096, hq=32, hkv=8, d=128, page=16,
+                    scaling="weak", layout="sequences", cascade=True,
+                    desc="cascade decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU sharing a "
+                         "4096-token prefix, 512 own tokens each")
     if name == "decode70b":
         # Tensor-parallel layout: KV heads sharded, one all-gather of the outputs per step.
         return dict(kind="decode", batch=256, ctx=8192, hq=64, hkv=8, d=128, page=16, scaling="strong",
@@ -296,6 +304,15 @@ def main() -> None:
             b_local = B
             q, kv = random_paged_pool([ctx] * B, hq, hkv, d, page, dtype=torch.bfloat16, device=dev, seed=1234,
                                       kv_head_slice=(lo, hi))
+        elif spec.get("cascade"):
+            from kernel_lab.kv_cache import PagedKV, random_cascade_problem
+
+            b_lo, b_hi = batch_range(B, world, rank)
+            b_local = b_hi - b_lo
+            q, ckv = random_cascade_problem([b_local], [spec["prefix"]], [ctx] * b_local, hq, hkv, d, page,
+                                            dtype=torch.bfloat16, device=dev, seed=1234 + rank)
+            kv = PagedKV(k_cache=ckv.k_cache, v_cache=ckv.v_cache, block_table=ckv.block_table,
+                         seq_lens=ckv.seq_lens, page_size=page)
         else:
             b_lo, b_hi = batch_range(B, world, rank)
             b_local = b_hi - b_lo
@@ -308,7 +325,21 @@ def main() -> None:
         kv_bytes = 1 if spec.get("kv8") else 2
         kernel_work = decode_attention_work([ctx] * b_local, hq_l, hkv_l, d, 2, kv_bytes)  # per rank, per launch
         job_bytes = decode_attention_work([ctx] * B, hq, hkv, d, 2, kv_bytes).bytes
-        if spec.get("kv8"):
+        if spec.get("cascade"):
+            from kernel_lab.roofline import Work
+
+            # Unique KV bytes: each GPU's shared prefix once plus every sequence's own tokens.
+            prefix_kv = spec["prefix"] * hkv * d * 2 * 2
+            kernel_work = Work(kernel_work.bytes + prefix_kv,
+                               kernel_work.flops + 4 * spec["prefix"] * b_local * hq * d)
+            job_bytes += prefix_kv * world
+        if spec.get("cascade"):
+
+            def decode_op(out_t, q_t, bt_t, ln_t):
+                torch.ops.kernel_lab.paged_decode_attention_cascade(
+                    out_t, q_t, kv.k_cache, kv.v_cache, ckv.prefix_block_table, ckv.prefix_lens, ckv.prefix_indptr,
+                    bt_t, ln_t, scale, None, None)
+        elif spec.get("kv8"):
             from kernel_lab.kv_cache import e4m3_scales, quantize_e4m3
 
             k_scale, v_scale = e4m3_scales(kv.k_cache), e4m3_scales(kv.v_cache)
@@ -332,7 +363,7 @@ def main() -> None:
             if gather:
                 gather_heads(out_local, world, out=out_full)
 
-        metric = FP8_METRIC if spec.get("kv8") else METRIC
+        metric = FP8_METRIC if spec.get("kv8") else CASCADE_METRIC if spec.get("cascade") else METRIC
     else:
         R, H = spec["rows"], spec["hidden"]
         g = torch.Generator(device=dev).manual_seed(7)
@@ -495,7 +526,8 @@ def main() -> None:
         traffic = load_traffic(key)
         value = job_bytes / (step_ms * 1e-3) / 1e9
         cpu = None
-        if world == 1 and not args.no_cpu_baseline and not spec.get("kv8"):  # kernel-lab has no e4m3 path
+        # kernel-lab has no e4m3 or cascade path to time on the host
+        if world == 1 and not args.no_cpu_baseline and not spec.get("kv8") and not spec.get("cascade"):
             cpu = cpu_measure(spec["kind"], spec, args.cpu_seconds)
         layout = spec.get("layout")
         parallelism = "1 gpu" if world == 1 else f"kv-head tp{world}" if layout == "kv_heads" else f"sequences dp{world}"
@@ -534,12 +566,14 @@ def main() -> None:
                 if peaks.source == "measured" else "fallback 6650 GB/s",
                 "traffic": traffic,
                 "algorithmic_bytes_per_launch": int(kernel_work.bytes),
-                "kernel": "decode_tc_kernel" if spec["kind"] == "decode" else "rmsnorm_row_regs",
+                "kernel": ("cascade_prefix_kernel + cascade_prefix_reduce_kernel + decode_tc_kernel (the whole op)"
+                           if spec.get("cascade") else "decode_tc_kernel" if spec["kind"] == "decode"
+                           else "rmsnorm_row_regs"),
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks.summary(),
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (3 if spec.get("cascade") else 1),
             "status_bits": status,
         }
         print(json.dumps(line), flush=True)

@@ -104,8 +104,15 @@ struct DecodeArgs {
   int64_t prefix_bt_stride;
   int prefix_max_pages;
   int members;    // sequences whose query rows one prefix item packs (a "member block")
-  float* cas_o;   // [2][batch * num_q_heads][head_dim]: normalised output of each side (0: prefix)
-  float* cas_lse; // [2][batch * num_q_heads]: base-2 LSE of each side
+  // Prefix chunks of prefix_chunk tokens computed by the tensor-core prefix kernel (0: the
+  // prefix items are entries of this kernel's plan, one chunk each). A sequence's state is merged
+  // from nch = ceil(prefix length / prefix_chunk) prefix planes (plane c: chunk c) and its own
+  // plane (cas_planes), by whichever of the nch + 1 arrivals comes last.
+  int prefix_chunk;
+  int cas_planes;
+  int cas_hpw;    // query rows per counter group (the decode kernel's heads per warp)
+  float* cas_o;   // [cas_planes + 1][batch * num_q_heads][head_dim]: normalised partial outputs
+  float* cas_lse; // [cas_planes + 1][batch * num_q_heads]: their base-2 LSEs
 };
 
 struct TcShape {
@@ -280,6 +287,7 @@ __device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps) {
       for (int p = tid; p < P; p += nt) clamp_prefix_len(a, p, true);
     }
   }
+  if (a.prefix_chunk > 0) V = 0;  // the prefix chunks run in the tensor-core prefix kernel
   const int n = V + B;
   for (int e = tid; e < n; e += nt) {
     ps.lens[e] = e < V ? clamp_prefix_len(a, group_of_entry(ps.vstart, a.num_prefixes, e), false)
@@ -446,8 +454,15 @@ __device__ __forceinline__ int64_t sink_row(const DecodeArgs& a, const RowSink& 
   return static_cast<int64_t>(k.seq + m) * a.num_q_heads + k.kvh * a.group + (r - m * a.group);
 }
 
+// Row offset of a cascade side's plane: the (single) prefix plane of an in-plan prefix item, or
+// the sequence's own plane after the prefix chunk planes.
 __device__ __forceinline__ int64_t side_offset(const DecodeArgs& a, int side) {
-  return static_cast<int64_t>(side) * a.batch * a.num_q_heads;
+  return static_cast<int64_t>(side == 0 ? 0 : a.cas_planes) * a.batch * a.num_q_heads;
+}
+
+// Prefix planes of sequence b's cascade, from its group's clamped prefix length.
+__device__ __forceinline__ int prefix_planes(const DecodeArgs& a, int prefix_len) {
+  return a.prefix_chunk > 0 ? (prefix_len + a.prefix_chunk - 1) / a.prefix_chunk : 1;
 }
 
 // Merge of a split (entry, unit, query-head group) by one warp, every chunk's normalised
@@ -597,30 +612,88 @@ __device__ __forceinline__ void merge_chunks(const DecodeArgs& a, const Seg& s, 
   }
 }
 
-// Final output of sequence b's query heads kvh * group + row0 .. + nh in a cascade, once both
-// sides (its group's shared prefix, its own tokens) have stored their normalised outputs and
-// LSEs: out = (2^(lse0 - M) o0 + 2^(lse1 - M) o1) / (2^(lse0 - M) + 2^(lse1 - M)), M the larger
-// LSE; the same arithmetic whichever side merges. One warp, lane-parallel over float4 columns.
-template <typename T, int D>
-__device__ __forceinline__ void cascade_merge(const DecodeArgs& a, int b, int kvh, int row0, int nh, int lane) {
+// Final output of sequence b's query heads kvh * group + row0 .. + nh in a cascade, once every
+// part has stored its normalised output and LSE: the nch prefix planes (chunks of its group's
+// shared prefix) and, if `own`, its own plane. One pass in plane order with a running maximum,
+// out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M): the same arithmetic whichever part arrives
+// last. One warp: lane L owns float4 columns L + 32 j of the nh x head_dim rows, and four planes'
+// loads are in flight at a time.
+template <typename T, int D, int NE>
+__device__ __forceinline__ void cascade_merge_impl(const DecodeArgs& a, int b, int kvh, int row0, int nh, int nch,
+                                                   bool own, int lane) {
   constexpr int Q = D / 4;
-  const int64_t plane = side_offset(a, 1);
+  constexpr int KB = 4;
+  const int n4 = nh * Q;
+  const int np = nch + (own ? 1 : 0);
+  const int64_t plane = static_cast<int64_t>(a.batch) * a.num_q_heads;
   const int64_t r0 = static_cast<int64_t>(b) * a.num_q_heads + kvh * a.group + row0;
+  float m[NE], wsum[NE];
+  float4 acc[NE];
+#pragma unroll
+  for (int j = 0; j < NE; ++j) {
+    m[j] = -INFINITY;
+    wsum[j] = 0.0f;
+    acc[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  for (int k0 = 0; k0 < np; k0 += KB) {
+    float l[KB][NE];
+    float4 x[KB][NE];
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+      const int k = k0 + q;
+      const int64_t off = static_cast<int64_t>(k < nch ? k : a.cas_planes) * plane;
+#pragma unroll
+      for (int j = 0; j < NE; ++j) {
+        const int i = lane + 32 * j;
+        const bool ld = k < np && i < n4;
+        const int h = i / Q;
+        l[q][j] = ld ? __ldcg(a.cas_lse + off + r0 + h) : -INFINITY;
+        x[q][j] = ld ? __ldcg(reinterpret_cast<const float4*>(a.cas_o + (off + r0 + h) * D) + (i - h * Q))
+                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+#pragma unroll
+      for (int j = 0; j < NE; ++j) {
+        const float mn = fmaxf(m[j], l[q][j]);
+        if (mn == -INFINITY) continue;
+        const float fa = fast_exp2(m[j] - mn), fb = fast_exp2(l[q][j] - mn);
+        m[j] = mn;
+        wsum[j] = wsum[j] * fa + fb;
+        acc[j].x = acc[j].x * fa + fb * x[q][j].x;
+        acc[j].y = acc[j].y * fa + fb * x[q][j].y;
+        acc[j].z = acc[j].z * fa + fb * x[q][j].z;
+        acc[j].w = acc[j].w * fa + fb * x[q][j].w;
+      }
+    }
+  }
   T* out = static_cast<T*>(a.out);
-  for (int i = lane; i < nh * Q; i += 32) {
-    const int h = i / Q, c4 = i - h * Q;
-    const int64_t row = r0 + h;
-    const float l0 = __ldcg(a.cas_lse + row), l1 = __ldcg(a.cas_lse + plane + row);
-    const float mx = fmaxf(l0, l1);
-    const float w0 = l0 > -INFINITY ? fast_exp2(l0 - mx) : 0.0f;
-    const float w1 = l1 > -INFINITY ? fast_exp2(l1 - mx) : 0.0f;
-    const float inv = w0 + w1 > 0.0f ? 1.0f / (w0 + w1) : 0.0f;
-    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a.cas_o + row * D) + c4);
-    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a.cas_o + (plane + row) * D) + c4);
+#pragma unroll
+  for (int j = 0; j < NE; ++j) {
+    const int i = lane + 32 * j;
+    if (i >= n4) continue;
+    const int h = i / Q;
+    const float inv = wsum[j] > 0.0f ? 1.0f / wsum[j] : 0.0f;
     uint2 pk;
-    pk.x = Storage<T>::pack2((w0 * x0.x + w1 * x1.x) * inv, (w0 * x0.y + w1 * x1.y) * inv);
-    pk.y = Storage<T>::pack2((w0 * x0.z + w1 * x1.z) * inv, (w0 * x0.w + w1 * x1.w) * inv);
-    *reinterpret_cast<uint2*>(out + row * D + 4 * c4) = pk;
+    pk.x = Storage<T>::pack2(acc[j].x * inv, acc[j].y * inv);
+    pk.y = Storage<T>::pack2(acc[j].z * inv, acc[j].w * inv);
+    *reinterpret_cast<uint2*>(out + (r0 + h) * D + 4 * (i - h * Q)) = pk;
+  }
+}
+
+template <typename T, int D>
+__device__ __forceinline__ void cascade_merge(const DecodeArgs& a, int b, int kvh, int row0, int nh, int nch,
+                                              bool own, int lane) {
+  constexpr int Q = D / 4;
+  if (nh * Q <= 128) {
+    cascade_merge_impl<T, D, 4>(a, b, kvh, row0, nh, nch, own, lane);
+  } else if (nh * Q <= 256) {
+    cascade_merge_impl<T, D, 8>(a, b, kvh, row0, nh, nch, own, lane);
+  } else {
+    for (int r = 0; r < nh; r += 256 / Q) {  // 256 float4 at a time
+      cascade_merge_impl<T, D, 8>(a, b, kvh, row0 + r, min(256 / Q, nh - r), nch, own, lane);
+    }
   }
 }
 
@@ -630,20 +703,23 @@ __device__ __forceinline__ void cascade_merge(const DecodeArgs& a, int b, int kv
 // group of the counter: a member's rows in it are its query heads grow0 .. grow0 + nh of the KV
 // head's group (grow0 = hg * heads per warp; a packed prefix item has one group).
 template <typename T, int D>
-__device__ __forceinline__ void cascade_arrive(const DecodeArgs& a, const RowSink& sink, int hg, int grow0, int nh,
-                                               int lane) {
+__device__ __forceinline__ void cascade_arrive(const DecodeArgs& a, const RowSink& sink, int hg,
+                                               int grow0, int nh, int lane) {
   __syncwarp();
-  bool second = false;
+  bool last = false;
   if (lane < sink.nmem && ((sink.cas >> lane) & 1u)) {
-    second = atom_add_acq_rel_gpu(counter_of(a, 2 * a.batch + sink.seq + lane, sink.kvh, hg), 1u) == 1u;
+    // The tensor-core prefix kernels ran before this launch: the prefix state is complete in
+    // plane 0 and this side is the last. Otherwise two sides count.
+    last = a.prefix_chunk > 0 ||
+           atom_add_acq_rel_gpu(counter_of(a, 2 * a.batch + sink.seq + lane, sink.kvh, hg), 1u) == 1u;
   }
-  uint32_t todo = __ballot_sync(0xffffffffu, second);
+  uint32_t todo = __ballot_sync(0xffffffffu, last);
   while (todo != 0u) {
     const int m = __ffs(todo) - 1;
     todo &= todo - 1u;
     __syncwarp();
-    cascade_merge<T, D>(a, sink.seq + m, sink.kvh, grow0, nh, lane);
-    if (lane == m) {
+    cascade_merge<T, D>(a, sink.seq + m, sink.kvh, grow0, nh, 1, true, lane);
+    if (lane == m && a.prefix_chunk == 0) {
       *reinterpret_cast<volatile uint32_t*>(counter_of(a, 2 * a.batch + sink.seq + m, sink.kvh, hg)) = 0u;
     }
   }
@@ -1387,6 +1463,405 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   }
 }
 
+// ------------------------------------------------------------------------- tensor-core prefix kernel
+//
+// The shared-prefix half of a cascade on the 5th-generation tensor cores. A prefix's keys are
+// read by every sequence of its group, so its attention is a real matrix product: 128 query rows
+// (128 / group sequences of one group, all query heads of one KV head) against the prefix's keys.
+// One CTA takes one (member block of 128 rows, KV head, chunk of kPrefixTokens prefix tokens):
+//   TMA brings Q (128 rows x head_dim), the chunk's K and V pages into 128-byte-swizzled tiles;
+//   one thread issues S = Q.K^T (M = 128 rows, N = chunk tokens, K = head_dim) into TMEM;
+//   each thread owns one row (one TMEM lane): exact softmax of its chunk, P written to shared
+//   memory as the next MMA's A operand;
+//   one thread issues O = P.V (N = head_dim, K = chunk tokens; V as an MN-major operand) into TMEM;
+//   each thread normalises its row and stores it, with its LSE, as prefix plane `chunk` of the
+//   row's sequence, then the cascade counter decides who merges (cascade_merge).
+// No online rescaling is needed: a chunk's softmax is exact within the chunk, and the chunks are
+// merged by their LSEs like any other split.
+
+constexpr int kPrefixTokens = 128;   // tokens of one chunk: the N of S = Q.K^T, the K of O = P.V
+constexpr int kPrefixThreads = 128;  // one thread per query row / TMEM lane
+
+struct PrefixLayout {
+  uint32_t q, k, v, p, bars, tptr, ints, total;
+};
+
+__host__ __device__ inline PrefixLayout prefix_layout(int D) {
+  constexpr uint32_t CT = kPrefixTokens;
+  const uint32_t nh = D / 64;
+  PrefixLayout L{};
+  L.q = 0;
+  L.k = L.q + nh * 128u * 128u;
+  L.v = L.k + nh * CT * 128u;
+  const uint32_t pbytes = 128u * CT * 2u;
+  const bool reuse = nh * CT * 128u >= pbytes;  // P overwrites K once S is computed
+  L.p = reuse ? L.k : L.v + nh * CT * 128u;
+  const uint32_t end = reuse ? L.v + nh * CT * 128u : L.p + pbytes;
+  L.bars = end;
+  L.tptr = end + 32u;
+  L.ints = end + 64u;
+  L.total = L.ints + 512u * 4u + 1024u;  // + slack to align the base to 1024 B
+  return L;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmq,
+                                                                           const __grid_constant__ CUtensorMap tmk,
+                                                                           const __grid_constant__ CUtensorMap tmv,
+                                                                           const DecodeArgs a) {
+  constexpr int CT = kPrefixTokens;
+  constexpr int NH = D / 64;                  // 128-byte column blocks of a head row
+  constexpr uint32_t QH = 128u * 128u;        // one column block of Q: 128 rows
+  constexpr uint32_t KH = CT * 128u;          // one column block of K or V: CT token rows
+  constexpr uint32_t PH = 128u * 128u;        // one 64-token column block of P: 128 rows
+  constexpr uint32_t NCOL = CT + D <= 256 ? 256u : 512u;
+  // At most two CTAs share an SM (shared memory), so their TMEM columns always fit in 512.
+  static_assert(NCOL <= 256u, "two co-resident CTAs must fit in the SM's 512 TMEM columns");
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_S = umma_idesc_f16(BF16, 128, CT, false);
+  constexpr uint32_t IDESC_O = umma_idesc_f16(BF16, 128, D, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const PrefixLayout L = prefix_layout(D);
+  const uint32_t base = smem_u32(smem);
+  const uint32_t sq = base + L.q, sk = base + L.k, sv = base + L.v, sp = base + L.p;
+  const uint32_t bar_qk = base + L.bars, bar_v = bar_qk + 8, bar_s = bar_qk + 16, bar_o = bar_qk + 24;
+  int* ints = reinterpret_cast<int*>(smem + L.ints);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = a.group, B = a.batch, P = a.page_size;
+  const int Mb = 128 / G;
+  const int chunk = blockIdx.x, kvh = blockIdx.y;
+
+  // ---- member block blockIdx.z: its group (a block scan over the groups' block counts)
+  {
+    const int ngrp = a.num_prefixes;
+    const int per = (ngrp + kPrefixThreads - 1) / kPrefixThreads;
+    const int lo = min(ngrp, tid * per), hi = min(ngrp, lo + per);
+    int local = 0;
+    bool bad = false;
+    for (int p = lo; p < hi; ++p) {
+      const int i0 = __ldg(a.prefix_indptr + p), i1 = __ldg(a.prefix_indptr + p + 1);
+      bad |= i0 > i1 || (p == 0 && i0 != 0) || (p == ngrp - 1 && i1 != B);
+      local += i1 > i0 ? (i1 - i0 + Mb - 1) / Mb : 0;
+    }
+    if (__syncthreads_or(bad)) return;  // the decode kernel reports it and ignores the prefixes
+    ints[tid] = local;
+    if (tid == 0) ints[300] = -1;
+    __syncthreads();
+    block_scan(kPrefixThreads, [&](int i) { return ints[i]; }, ints + 128, ints + 260);
+    const int first = ints[128 + tid];
+    const int z = blockIdx.z;
+    if (z >= first && z < first + local) {
+      int acc = first;
+      for (int p = lo; p < hi; ++p) {
+        const int i0 = __ldg(a.prefix_indptr + p), i1 = __ldg(a.prefix_indptr + p + 1);
+        const int nb = i1 > i0 ? (i1 - i0 + Mb - 1) / Mb : 0;
+        if (z < acc + nb) {
+          const int b0 = i0 + (z - acc) * Mb;
+          ints[300] = p;
+          ints[301] = b0;
+          ints[302] = min(Mb, i1 - b0);
+          break;
+        }
+        acc += nb;
+      }
+    }
+    __syncthreads();
+  }
+  const int grp = ints[300];
+  if (grp < 0) return;
+  const int b0 = ints[301], nmem = ints[302];
+  const int plen = clamp_prefix_len(a, grp, false);
+  const int tok0 = chunk * CT;
+  if (tok0 >= plen) return;
+  const int ntok = min(CT, plen - tok0);
+  const int nch = (plen + CT - 1) / CT;
+  const int npg = (ntok + P - 1) / P;  // pages of this chunk (CT is a multiple of the page size)
+  // One parallel round of small loads: the chunk's page ids (-1: outside the pool) and the
+  // block's sequences' own lengths.
+  int* s_page = ints + 320;
+  int* s_own = ints + 352;
+  if (tid < npg) {
+    const int page = __ldg(a.prefix_bt + static_cast<int64_t>(grp) * a.prefix_bt_stride + tok0 / P + tid);
+    s_page[tid] = (page < 0 || (a.num_pages >= 0 && page >= a.num_pages)) ? -1 : page;
+  }
+  if (tid < nmem) s_own[tid] = clamp_len(a, b0 + tid, false);
+  if (tid == 0) {
+    mbar_init(bar_qk, 1);
+    mbar_init(bar_v, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();  // tcgen05.alloc is .sync.aligned: the whole warp, converged
+  if (warp == 0) {
+    tmem_alloc(base + L.tptr, NCOL);
+    tmem_relinquish();
+  }
+  tcgen05_fence_before();
+  __syncthreads();
+  tcgen05_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L.tptr);
+  const uint32_t tS = tmem, tO = tmem + CT;
+  // Pages outside the pool are skipped (flagged); their K and V rows are zeroed so that stale
+  // shared memory cannot enter the product.
+  uint32_t badmask = 0;
+  for (int pg = 0; pg < npg; ++pg) badmask |= s_page[pg] < 0 ? 1u << pg : 0u;
+  if (badmask != 0u) {
+    if (tid == 0) atomicOr(a.sync, kStatusBadPage);
+    for (int pg = 0; pg < npg; ++pg) {
+      if (!((badmask >> pg) & 1u)) continue;
+      for (int i = tid; i < NH * P * 8; i += kPrefixThreads) {  // 16-byte units of the page's rows
+        const int h = i / (P * 8), r = (i / 8) % P, u = i % 8;
+        const uint32_t off = h * KH + (pg * P + r) * 128u + u * 16u;
+        sts128(sk + off, make_uint4(0u, 0u, 0u, 0u));
+        sts128(sv + off, make_uint4(0u, 0u, 0u, 0u));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
+  bool ok = true;
+
+  if (warp == 0) {
+    // Lane i issues page i's boxes (both tensors, every column block); lane h < NH issues Q's.
+    const uint64_t pol = l2_policy_evict_normal();
+    const int page = lane < npg ? s_page[lane] : -1;
+    const uint32_t nvalid = static_cast<uint32_t>(__popc(__ballot_sync(0xffffffffu, page >= 0)));
+    const uint32_t kv_bytes = nvalid * NH * P * 128u;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar_qk, NH * QH + kv_bytes);
+      mbar_arrive_expect_tx(bar_v, kv_bytes);
+    }
+    __syncwarp();
+    if (lane < NH) tma_load_3d(sq + lane * QH, &tmq, lane * 64, kvh * G, b0, bar_qk, pol);
+    if (page >= 0) {
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        tma_load_3d(sk + h * KH + lane * P * 128u, &tmk, 0, kvh * NH + h, page * P, bar_qk, pol);
+      }
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        tma_load_3d(sv + h * KH + lane * P * 128u, &tmv, 0, kvh * NH + h, page * P, bar_v, pol);
+      }
+    }
+  }
+  if (tid == 0) {
+    // S = Q . K^T: K = head_dim in steps of 16 (32 bytes of a 128-byte row; column block ks / 4).
+    ok = mbar_wait_bounded(bar_qk, 0, a.sync, kWaitLimit);
+    if (ok) {
+      tcgen05_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint32_t off = (ks % 4) * 32u;
+        const uint64_t ad = umma_desc_sw128(sq + (ks / 4) * QH + off, 16u, 1024u);
+        const uint64_t bd = umma_desc_sw128(sk + (ks / 4) * KH + off, 16u, 1024u);
+        umma_f16(tS, ad, bd, IDESC_S, ks > 0 ? 1u : 0u);
+      }
+    }
+    umma_commit(bar_s);  // also when nothing was issued: the barrier still completes
+  }
+
+  // ---- softmax of this thread's row over the chunk (exact within the chunk)
+  ok = mbar_wait_bounded(bar_s, 0, a.sync, kWaitLimit) && ok;
+  tcgen05_fence_after();
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const float sl = a.scale_log2;
+  // The whole row of S at once (CT columns, one TMEM round trip), kept in registers for both passes.
+  uint32_t sr[CT / 32][32];
+#pragma unroll
+  for (int cc = 0; cc < CT / 32; ++cc) tmem_ld32(tS + lane_base + cc * 32, sr[cc]);
+  tmem_wait_ld();
+  float mx = -INFINITY;
+#pragma unroll
+  for (int cc = 0; cc < CT / 32; ++cc) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (cc * 32 + i < ntok) mx = fmaxf(mx, __uint_as_float(sr[cc][i]) * sl);
+    }
+  }
+  float lsum = 0.0f;
+#pragma unroll
+  for (int cc = 0; cc < CT / 32; ++cc) {
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) {  // 8 tokens: one 16-byte unit of P's row
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t0 = cc * 32 + q8 * 8 + 2 * j;
+        const float p0 = t0 < ntok ? fast_exp2(__uint_as_float(sr[cc][q8 * 8 + 2 * j]) * sl - mx) : 0.0f;
+        const float p1 = t0 + 1 < ntok ? fast_exp2(__uint_as_float(sr[cc][q8 * 8 + 2 * j + 1]) * sl - mx) : 0.0f;
+        w[j] = Storage<T>::pack2(p0, p1);
+        const float2 f = Storage<T>::unpack2(w[j]);  // the normaliser sums what the MMA uses
+        lsum += f.x + f.y;
+      }
+      const int tok = cc * 32 + q8 * 8;
+      const uint32_t unit = static_cast<uint32_t>((tok % 64) / 8) ^ static_cast<uint32_t>(tid & 7);
+      sts128(sp + (tok / 64) * PH + tid * 128u + (unit << 4), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  }
+  // V rows past the chunk's tokens (a page's tail) are zeroed: P is zero there, but 0 * NaN is not.
+  ok = mbar_wait_bounded(bar_v, 0, a.sync, kWaitLimit) && ok;
+  for (int i = tid; i < NH * (CT - ntok) * 8; i += kPrefixThreads) {
+    const int h = i / ((CT - ntok) * 8), r = ntok + (i / 8) % (CT - ntok), u = i % 8;
+    sts128(sv + h * KH + r * 128u + u * 16u, make_uint4(0u, 0u, 0u, 0u));
+  }
+  fence_proxy_async_smem();
+  tcgen05_fence_before();
+  __syncthreads();
+
+  if (tid == 0) {
+    tcgen05_fence_after();
+    if (ok) {
+      // O = P . V: K = chunk tokens in steps of 16; A = P (K-major, 64-token column blocks),
+      // B = V as an MN-major operand (rows = tokens, 64-element column blocks KH bytes apart).
+#pragma unroll
+      for (int ks = 0; ks < CT / 16; ++ks) {
+        const uint64_t ad = umma_desc_sw128(sp + (ks / 4) * PH + (ks % 4) * 32u, 16u, 1024u);
+        const uint64_t bd = umma_desc_sw128(sv + ks * 16u * 128u, KH, 1024u);
+        umma_f16(tO, ad, bd, IDESC_O, ks > 0 ? 1u : 0u);
+      }
+    }
+    umma_commit(bar_o);
+  }
+  ok = mbar_wait_bounded(bar_o, 0, a.sync, kWaitLimit) && ok;
+  ok = __syncthreads_and(ok);  // one verdict for the CTA (only thread 0 waited on the loads)
+  tcgen05_fence_after();
+
+  // ---- epilogue: row tid = member m, query head gi of KV head kvh. A sequence whose prefix is
+  // this one chunk and that has no tokens of its own gets its final output here; otherwise the
+  // row becomes prefix plane `chunk` (collapsed by cascade_prefix_reduce_kernel when the prefix
+  // has several chunks, merged with the sequence's own tokens by the decode kernel).
+  const int m = tid / G, gi = tid - m * G;
+  const bool valid = ok && m < nmem;
+  const bool direct = valid && nch == 1 && s_own[m] == 0;
+  const int64_t row = static_cast<int64_t>(b0 + m) * a.num_q_heads + kvh * G + gi;
+  const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+  const float lse = lsum > 0.0f ? mx + __log2f(lsum) : -INFINITY;
+  uint32_t orr[D / 32][32];
+  __syncwarp();  // tcgen05.ld is .sync.aligned
+#pragma unroll
+  for (int cc = 0; cc < D / 32; ++cc) tmem_ld32(tO + lane_base + cc * 32, orr[cc]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int cc = 0; cc < D / 32; ++cc) {
+    const uint32_t(&r)[32] = orr[cc];
+    if (!valid) continue;
+    if (direct) {
+      T* dst = static_cast<T*>(a.out) + row * D + cc * 32;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 pk;
+        pk.x = Storage<T>::pack2(__uint_as_float(r[8 * j + 0]) * inv, __uint_as_float(r[8 * j + 1]) * inv);
+        pk.y = Storage<T>::pack2(__uint_as_float(r[8 * j + 2]) * inv, __uint_as_float(r[8 * j + 3]) * inv);
+        pk.z = Storage<T>::pack2(__uint_as_float(r[8 * j + 4]) * inv, __uint_as_float(r[8 * j + 5]) * inv);
+        pk.w = Storage<T>::pack2(__uint_as_float(r[8 * j + 6]) * inv, __uint_as_float(r[8 * j + 7]) * inv);
+        reinterpret_cast<uint4*>(dst)[j] = pk;
+      }
+    } else {
+      float4* dst = reinterpret_cast<float4*>(
+          a.cas_o + (static_cast<int64_t>(chunk) * B * a.num_q_heads + row) * D + cc * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        dst[j] = make_float4(__uint_as_float(r[4 * j]) * inv, __uint_as_float(r[4 * j + 1]) * inv,
+                             __uint_as_float(r[4 * j + 2]) * inv, __uint_as_float(r[4 * j + 3]) * inv);
+      }
+    }
+  }
+  if (valid && !direct) a.cas_lse[static_cast<int64_t>(chunk) * B * a.num_q_heads + row] = lse;
+  tcgen05_fence_before();
+  __syncthreads();  // every TMEM read done
+  if (warp == 0) {
+    __syncwarp();
+    tmem_dealloc(tmem, NCOL);
+  }
+}
+
+// Collapses the prefix chunk planes of every sequence whose group's prefix has several chunks into
+// plane 0 (output and LSE); a sequence without tokens of its own gets its final output instead.
+// Runs between the prefix kernel and the decode kernel. One block per query row: its 256 threads
+// form kReduceStreams streams of head_dim / 4 threads (one float4 column each); stream s walks
+// planes s, s + kReduceStreams, ... with a running maximum and four planes' loads in flight; the
+// streams' (max, weight, sum) are then combined in stream order, so the result is deterministic.
+constexpr int kReduceThreads = 256;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kReduceThreads) cascade_prefix_reduce_kernel(const DecodeArgs a) {
+  constexpr int Q = D / 4;
+  constexpr int NS = kReduceThreads / Q;  // streams
+  constexpr int KB = 4;
+  __shared__ float s_m[NS][Q], s_w[NS][Q];
+  __shared__ float4 s_o[NS][Q];
+  const int64_t row = blockIdx.x;
+  const int b = static_cast<int>(row / a.num_q_heads);
+  int lo = 0, hi = a.num_prefixes - 1;  // last group starting at or before b
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(a.prefix_indptr + mid) <= b) lo = mid; else hi = mid - 1;
+  }
+  const int nch = prefix_planes(a, clamp_prefix_len(a, lo, false));
+  if (nch <= 1) return;  // uniform over the block
+  const int st = threadIdx.x / Q, c4 = threadIdx.x % Q;
+  const int64_t plane = static_cast<int64_t>(a.batch) * a.num_q_heads;
+  float mx = -INFINITY, wsum = 0.0f;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int k0 = st; k0 < nch; k0 += NS * KB) {
+    float l[KB];
+    float4 x[KB];
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+      const int k = k0 + q * NS;
+      l[q] = k < nch ? __ldcg(a.cas_lse + k * plane + row) : -INFINITY;
+      x[q] = k < nch ? __ldcg(reinterpret_cast<const float4*>(a.cas_o + (k * plane + row) * D) + c4)
+                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int q = 0; q < KB; ++q) {
+      const float mn = fmaxf(mx, l[q]);
+      if (mn == -INFINITY) continue;
+      const float fa = fast_exp2(mx - mn), fb = fast_exp2(l[q] - mn);
+      mx = mn;
+      wsum = wsum * fa + fb;
+      acc.x = acc.x * fa + fb * x[q].x;
+      acc.y = acc.y * fa + fb * x[q].y;
+      acc.z = acc.z * fa + fb * x[q].z;
+      acc.w = acc.w * fa + fb * x[q].w;
+    }
+  }
+  s_m[st][c4] = mx;
+  s_w[st][c4] = wsum;
+  s_o[st][c4] = acc;
+  __syncthreads();  // every plane read (plane 0 included) before plane 0 is replaced
+  if (st != 0) return;
+  float m = -INFINITY, w = 0.0f;
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+  for (int t = 0; t < NS; ++t) {
+    const float mt = s_m[t][c4];
+    const float mn = fmaxf(m, mt);
+    if (mn == -INFINITY) continue;
+    const float fa = fast_exp2(m - mn), fb = fast_exp2(mt - mn);
+    const float4 ot = s_o[t][c4];
+    m = mn;
+    w = w * fa + fb * s_w[t][c4];
+    o.x = o.x * fa + fb * ot.x;
+    o.y = o.y * fa + fb * ot.y;
+    o.z = o.z * fa + fb * ot.z;
+    o.w = o.w * fa + fb * ot.w;
+  }
+  const float inv = w > 0.0f ? 1.0f / w : 0.0f;
+  if (clamp_len(a, b, false) == 0) {
+    uint2 pk;
+    pk.x = Storage<T>::pack2(o.x * inv, o.y * inv);
+    pk.y = Storage<T>::pack2(o.z * inv, o.w * inv);
+    *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + row * D + 4 * c4) = pk;
+    return;
+  }
+  reinterpret_cast<float4*>(a.cas_o + row * D)[c4] = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  if (c4 == 0) a.cas_lse[row] = w > 0.0f ? m + __log2f(w) : -INFINITY;
+}
+
 // ------------------------------------------------------------------------- generic kernel
 
 struct GenLayout {
@@ -1596,6 +2071,9 @@ struct Plan {
   bool kv8 = false;
   int groups = 0;   // cascade: prefix groups (0: plain decode)
   int members = 1;  // cascade: sequences packed into one prefix item
+  int prefix_chunk = 0;  // cascade: tokens per tensor-core prefix chunk (0: prefix items in the plan)
+  int cas_planes = 1;    // cascade: prefix planes per sequence (chunks of the longest prefix)
+  size_t prefix_smem = 0;
   size_t cas_o_off = 0, cas_lse_off = 0;  // cascade: side states within the partials buffer
   size_t part_bytes = 0, sync_bytes = 0;
   const void* fn = nullptr;
@@ -1732,6 +2210,17 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   p.tc = !generic && dtype != KL_FLOAT32 && (D == (kv8 ? 128 : 64) || D == 128 || D == 256) &&
          (P == 8 || P % 16 == 0) && HG > 0;
   if (kv8 && !p.tc) return static_cast<int>(cudaErrorInvalidValue);
+  // Cascade prefixes on the tensor-core prefix kernel when its shapes fit (KL_DECODE_CASCADE_TC=0
+  // keeps them in the decode kernel's plan): 16-bit cache, head_dim 64 or 128, a group size that
+  // divides the 128 rows of an MMA, and pages that tile a chunk.
+  if (cascade) {
+    const char* tc_env = std::getenv("KL_DECODE_CASCADE_TC");
+    const bool tc_prefix = !(tc_env && std::atoi(tc_env) == 0) && !kv8 && (D == 64 || D == 128) && 128 % G == 0 &&
+                           P <= kPrefixTokens && kPrefixTokens % P == 0;
+    p.prefix_chunk = tc_prefix ? kPrefixTokens : 0;
+    p.cas_planes = tc_prefix ? static_cast<int>(std::max<int64_t>(1, (prefix_tokens + kPrefixTokens - 1) / kPrefixTokens)) : 1;
+  }
+  const int64_t plan_prefix_tiles = p.prefix_chunk > 0 ? 0 : prefix_tiles;  // prefix tiles in the decode plan
   p.kv8 = kv8;
   const int eb = kv8 ? 1 : 2;
   int threads;
@@ -1741,7 +2230,7 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     // at most 64 KB, and enough (sequence, head-block) tiles to keep every SM busy.
     int ht = 1;
     while (ht * 2 <= 8 / HG && Hkv % (ht * 2) == 0 && ht * 2 * D <= 1024) ht *= 2;
-    const int64_t tiles = static_cast<int64_t>(batch) * (max_tiles + prefix_tiles);
+    const int64_t tiles = static_cast<int64_t>(batch) * (max_tiles + plan_prefix_tiles);
     while (ht > 1 && tiles * (Hkv / ht) < 4LL * sms) ht /= 2;
     const int forced_ht = env_int("KL_DECODE_HEADS_PER_TILE");
     if (forced_ht > 0 && forced_ht <= 8 / HG && Hkv % forced_ht == 0 && (forced_ht & (forced_ht - 1)) == 0 &&
@@ -1806,7 +2295,7 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   const int forced_cost = env_int("KL_DECODE_SEGMENT_COST");
   p.seg_cost = forced_cost < 0 ? 0 : forced_cost > 0 ? std::min(forced_cost, 64) : p.tc ? kTcSegmentCost : 0;
   const int64_t cost = static_cast<int64_t>(batch) * (max_tiles + p.seg_cost) +
-                       (cascade ? static_cast<int64_t>(batch) * (prefix_tiles + p.seg_cost) : 0);
+                       (cascade ? static_cast<int64_t>(batch) * (plan_prefix_tiles + p.seg_cost) : 0);
   if (cost * p.units > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
   p.slots = static_cast<int>(chunks * slots_per_chunk);
   p.part_bytes = lse_offset(p.slots, p.slot_heads, D) + static_cast<size_t>(p.slots) * p.slot_heads * 4;
@@ -1814,9 +2303,18 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
   p.sync_bytes = (1 + static_cast<size_t>(cascade ? 3 : 1) * batch * Hkv * kMaxHeadGroups) * 4;
   if (cascade) {
     const size_t rows = static_cast<size_t>(batch) * Hq;
+    const size_t planes = static_cast<size_t>(p.cas_planes) + 1;  // prefix planes + the sequences' own
     p.cas_o_off = (p.part_bytes + 255) / 256 * 256;
-    p.cas_lse_off = p.cas_o_off + 2 * rows * D * 4;
-    p.part_bytes = p.cas_lse_off + 2 * rows * 4;
+    p.cas_lse_off = p.cas_o_off + planes * rows * D * 4;
+    p.part_bytes = p.cas_lse_off + planes * rows * 4;
+    if (p.prefix_chunk > 0) {
+      p.prefix_smem = prefix_layout(D).total;
+      const void* pf = dtype == KL_FLOAT16 ? (D == 64 ? (const void*)cascade_prefix_kernel<__half, 64>
+                                                      : (const void*)cascade_prefix_kernel<__half, 128>)
+                                           : (D == 64 ? (const void*)cascade_prefix_kernel<__nv_bfloat16, 64>
+                                                      : (const void*)cascade_prefix_kernel<__nv_bfloat16, 128>);
+      if (blocks_per_sm(dev, pf, kPrefixThreads, p.prefix_smem) <= 0) return static_cast<int>(cudaErrorInvalidConfiguration);
+    }
   }
   return 0;
 }
@@ -1842,7 +2340,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 // p_rows tokens is one tile (or half of one, for page size 8) of a head block: for HT == Hkv a
 // whole page, read front to back.
 bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_tokens, int Hkv, int D, int HT,
-                   int p_rows, bool kv8) {
+                   int p_rows, bool kv8, int box_pieces = 0) {
   auto enc = encoder();
   if (!enc) return false;
   // 128-byte pieces: 64 two-byte elements, or 128 e4m3 bytes (moved as uint8).
@@ -1851,7 +2349,7 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_t
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(per_piece), static_cast<cuuint64_t>(row_bytes / 128),
                               static_cast<cuuint64_t>(pool_tokens)};
   const cuuint64_t strides[2] = {128u, static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(per_piece), static_cast<cuuint32_t>(HT * D * (kv8 ? 1 : 2) / 128),
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(per_piece), static_cast<cuuint32_t>(box_pieces > 0 ? box_pieces : HT * D * (kv8 ? 1 : 2) / 128),
                              static_cast<cuuint32_t>(p_rows)};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUtensorMapDataType dt = kv8                  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
@@ -1860,6 +2358,21 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int dtype, int64_t pool_t
   const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// q as the A operand of the prefix kernel: (64 elements = 128 bytes) x (query heads) x (sequences);
+// a box of 64 x group x 128/group is one 128-byte column block of a member block's 128 rows.
+bool encode_q_map(CUtensorMap* map, const void* q, int dtype, int batch, int Hq, int D, int G) {
+  auto enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Hq), static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2u, static_cast<cuuint64_t>(Hq) * D * 2u};
+  const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(128 / G)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = enc(map, dtype == KL_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                         const_cast<void*>(q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1971,9 +2484,45 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   a.prefix_bt_stride = cas.bt_stride;
   a.prefix_max_pages = cas.max_pages;
   a.members = p.members;
+  a.prefix_chunk = p.prefix_chunk;
+  a.cas_planes = p.cas_planes;
+  a.cas_hpw = 8 * p.NT;
   if (cascade) {
     a.cas_o = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + p.cas_o_off);
     a.cas_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(partials) + p.cas_lse_off);
+  }
+
+  if (use_tc && p.prefix_chunk > 0) {
+    // The shared prefixes first, on the tensor-core prefix kernel (one CTA per member block, KV
+    // head and chunk; CTAs past the real ones exit at once), then the sequences' own tokens.
+    CUtensorMap tmq, tpk, tpv;
+    const int64_t pool_tokens = num_pages >= 0 ? std::max<int64_t>(num_pages, 1) * P : (int64_t(1) << 31) - 1;
+    const int G = Hq / Hkv;
+    if (!encode_q_map(&tmq, q, dtype, batch, Hq, D, G) ||
+        !encode_kv_map(&tpk, k_cache, dtype, pool_tokens, Hkv, D, 1, P, false, 1) ||
+        !encode_kv_map(&tpv, v_cache, dtype, pool_tokens, Hkv, D, 1, P, false, 1)) {
+      return static_cast<int>(cudaErrorInvalidValue);
+    }
+    const dim3 grid(p.cas_planes, Hkv, (batch + 128 / G - 1) / (128 / G) + cas.groups);
+    if (dtype == KL_FLOAT16) {
+      if (D == 64) cascade_prefix_kernel<__half, 64><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
+      else cascade_prefix_kernel<__half, 128><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
+    } else {
+      if (D == 64) cascade_prefix_kernel<__nv_bfloat16, 64><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
+      else cascade_prefix_kernel<__nv_bfloat16, 128><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
+    }
+    if (const cudaError_t e = cudaGetLastError(); e != cudaSuccess) return static_cast<int>(e);
+    if (p.cas_planes > 1) {
+      const unsigned rows = static_cast<unsigned>(batch) * static_cast<unsigned>(Hq);  // one block per query row
+      if (dtype == KL_FLOAT16) {
+        if (D == 64) cascade_prefix_reduce_kernel<__half, 64><<<rows, kReduceThreads, 0, st>>>(a);
+        else cascade_prefix_reduce_kernel<__half, 128><<<rows, kReduceThreads, 0, st>>>(a);
+      } else {
+        if (D == 64) cascade_prefix_reduce_kernel<__nv_bfloat16, 64><<<rows, kReduceThreads, 0, st>>>(a);
+        else cascade_prefix_reduce_kernel<__nv_bfloat16, 128><<<rows, kReduceThreads, 0, st>>>(a);
+      }
+      if (const cudaError_t e = cudaGetLastError(); e != cudaSuccess) return static_cast<int>(e);
+    }
   }
 
   if (use_tc) {

@@ -19,6 +19,17 @@ from tests.conftest import assert_within_abs_or_ulp
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=["tensor_core_prefix", "prefix_in_plan"])
+def prefix_path(request, monkeypatch):
+    """Both ways a prefix is computed: the tcgen05 prefix kernel (the default where its shapes
+    fit) and prefix items inside the decode kernel's plan (KL_DECODE_CASCADE_TC=0)."""
+    if request.param == "prefix_in_plan":
+        monkeypatch.setenv("KL_DECODE_CASCADE_TC", "0")
+    else:
+        monkeypatch.delenv("KL_DECODE_CASCADE_TC", raising=False)
+    return request.param
+
 KL_STATUS_BAD_PAGE = 1
 KL_STATUS_BAD_PREFIX_GROUPS = 8
 
@@ -70,7 +81,7 @@ CASES = [
 
 @pytest.mark.parametrize("case", range(len(CASES)))
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_cascade_matches_the_oracle(case, dtype):
+def test_cascade_matches_the_oracle(case, dtype, prefix_path):
     from kernel_lab import cuda_ops
 
     groups, plens, lens, hq, hkv, d, page = CASES[case]
@@ -82,7 +93,7 @@ def test_cascade_matches_the_oracle(case, dtype):
     assert_within_abs_or_ulp(got, _oracle(q, kv), dtype)
 
 
-def test_cascade_is_deterministic_and_leaves_scratch_reusable():
+def test_cascade_is_deterministic_and_leaves_scratch_reusable(prefix_path):
     """Same inputs, same bits, whichever side of a cascade finishes second; a second call on
     the same scratch (counters returned to zero) gives the same result."""
     from kernel_lab import capi
@@ -99,7 +110,7 @@ def test_cascade_is_deterministic_and_leaves_scratch_reusable():
     assert scratch.status(clear=True) == 0
 
 
-def test_cascade_equals_plain_decode_over_concatenated_tables_at_serving_size():
+def test_cascade_equals_plain_decode_over_concatenated_tables_at_serving_size(prefix_path):
     """Headline shapes: 64 sequences share a 4096-token prefix and own 512 tokens each. The same
     problem without sharing (each row lists the prefix pages, then its own) through the plain
     decode op agrees within the two kernels' combined rounding."""
@@ -113,7 +124,7 @@ def test_cascade_equals_plain_decode_over_concatenated_tables_at_serving_size():
     assert (got.float() - ref.float()).abs().max().item() <= 2e-2
 
 
-def test_cascade_with_bad_groups_ignores_prefixes_and_says_so():
+def test_cascade_with_bad_groups_ignores_prefixes_and_says_so(prefix_path):
     from kernel_lab import cuda_ops
 
     q, kv = _problem([2, 2], [64, 32], [10, 20, 30, 40], 32, 8, 128, 16, torch.bfloat16, seed=4)
@@ -125,7 +136,7 @@ def test_cascade_with_bad_groups_ignores_prefixes_and_says_so():
     assert_within_abs_or_ulp(got, _oracle(q, kv), torch.bfloat16)
 
 
-def test_cascade_bad_prefix_page_is_skipped_and_flagged():
+def test_cascade_bad_prefix_page_is_skipped_and_flagged(prefix_path):
     from kernel_lab import cuda_ops
 
     q, kv = _problem([3], [64], [10, 20, 30], 32, 8, 128, 16, torch.bfloat16, seed=6)
