@@ -22,12 +22,9 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(params=["tensor_core_prefix", "prefix_in_plan"])
 def prefix_path(request, monkeypatch):
-    """Both ways a prefix is computed: the tcgen05 prefix kernel (the default where its shapes
-    fit) and prefix items inside the decode kernel's plan (KL_DECODE_CASCADE_TC=0)."""
-    if request.param == "prefix_in_plan":
-        monkeypatch.setenv("KL_DECODE_CASCADE_TC", "0")
-    else:
-        monkeypatch.delenv("KL_DECODE_CASCADE_TC", raising=False)
+    """Both ways a prefix is computed, forced: the tcgen05 prefix kernel (KL_DECODE_CASCADE_TC=1,
+    where its shapes fit) and prefix items inside the decode kernel's plan (=0)."""
+    monkeypatch.setenv("KL_DECODE_CASCADE_TC", "0" if request.param == "prefix_in_plan" else "1")
     return request.param
 
 KL_STATUS_BAD_PAGE = 1
