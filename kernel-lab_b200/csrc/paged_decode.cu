@@ -2194,9 +2194,10 @@ const void* gen_fn(int dtype) {
 constexpr uint32_t kTcSmemBudget = 225 * 1024;  // one tensor-core CTA per SM (227 KB is the limit)
 constexpr int kMaxStages = 24;
 // Balanced plan: tiles' worth of time a tensor-core CTA loses per (sequence, head block) it
-// starts (Q loads, partial write and count). Measured at batch 64 x 4096 tokens: charging 2
-// tiles levels CTAs with one and two segments (158.4 us against 160.4 us with none).
-constexpr int kTcSegmentCost = 2;
+// starts (Q loads, partial write and count). Charging 4 (sweep of 2..8, one box): batch 64 x 512
+// tokens 29.0 us against 31.1 us with 2, batch 8 x 512 16.7 against 18.8; batch 64 x 4096,
+// 256 x 512 and the 70B shape within 1 us of the cost-2 plan.
+constexpr int kTcSegmentCost = 4;
 
 // Optional tuning overrides read once from the environment:
 //   KL_DECODE_HEADS_PER_TILE (1/2/4/8), KL_DECODE_STAGES (2..24), KL_DECODE_SEGMENT_COST
