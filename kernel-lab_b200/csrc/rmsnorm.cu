@@ -15,8 +15,16 @@
 //
 // Rows that are misaligned, of odd width or wider than the register budget use
 // a two-pass fallback that re-reads its own row (from L2) for the output pass.
+//
+// Small batches (a decode step's 1-256 rows) are latency-bound: the kernel is a few µs and the
+// launch itself a sizeable part of it. Both kernels are launched with programmatic stream
+// serialization: a kernel may start while the previous kernel in the stream finishes, waits
+// (griddepcontrol.wait) before its first global read until that kernel has completed and its
+// writes are visible, and lets the next kernel launch (griddepcontrol.launch_dependents) once
+// its row is reduced. Results are the same; only the gap between kernels shrinks.
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 
 #include <cuda_runtime.h>
 
@@ -34,6 +42,11 @@ struct Pack16 {
     T v[N];
   };
 };
+
+// Programmatic dependent launch: wait for the previous kernel in the stream (no-op when it has
+// finished, or when this kernel was launched without the attribute); let the next one launch.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Sum over the block; every thread gets the total. `red` holds one float per warp.
 __device__ __forceinline__ float block_allreduce_sum(float v, float* red) {
@@ -64,6 +77,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_regs(T* __restrict__ out, co
 
   P a[NPT];
   P r[NPT];
+  wait_prior_grid();
 #pragma unroll
   for (int i = 0; i < NPT; ++i) {
     const int pk = threadIdx.x + i * blockDim.x;
@@ -94,6 +108,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_regs(T* __restrict__ out, co
   }
 
   const float rstd = 1.0f / sqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
+  allow_next_grid();
 
 #pragma unroll
   for (int i = 0; i < NPT; ++i) {
@@ -122,6 +137,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_twopass(T* __restrict__ out,
   T* rr = residual + row * static_cast<int64_t>(hidden);
   T* orow = out + row * static_cast<int64_t>(hidden);
 
+  wait_prior_grid();
   float ss = 0.0f;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
     float f;
@@ -135,6 +151,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_twopass(T* __restrict__ out,
     ss = fmaf(f, f, ss);
   }
   const float rstd = 1.0f / sqrtf(block_allreduce_sum(ss, red) / static_cast<float>(hidden) + eps);
+  allow_next_grid();
   const T* src = RES ? rr : xr;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
     orow[i] = Storage<T>::store((Storage<T>::load(src[i]) * rstd) * Storage<T>::load(weight[i]));
@@ -143,18 +160,42 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_twopass(T* __restrict__ out,
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// KL_RMSNORM_PDL=0 launches without programmatic stream serialization (read once).
+bool use_pdl() {
+  static const bool on = [] {
+    const char* v = std::getenv("KL_RMSNORM_PDL");
+    return !(v && std::atoi(v) == 0);
+  }();
+  return on;
+}
+
+// One CTA per row, `threads` threads, on `stream`, with programmatic stream serialization.
+template <typename... Params, typename... Args>
+cudaError_t launch_rows(void (*kernel)(Params...), int rows, int threads, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = use_pdl() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 template <typename T, int NPT>
-void launch_regs(void* out, const void* x, void* residual, const void* weight, int rows, int hidden,
-                 int64_t x_row_stride, float eps, cudaStream_t stream, int threads) {
+cudaError_t launch_regs(void* out, const void* x, void* residual, const void* weight, int rows, int hidden,
+                        int64_t x_row_stride, float eps, cudaStream_t stream, int threads) {
   auto o = static_cast<T*>(out);
   auto xi = static_cast<const T*>(x);
   auto r = static_cast<T*>(residual);
   auto w = static_cast<const T*>(weight);
   if (residual) {
-    rmsnorm_row_regs<T, NPT, true><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
-  } else {
-    rmsnorm_row_regs<T, NPT, false><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
+    return launch_rows(rmsnorm_row_regs<T, NPT, true>, rows, threads, stream, o, xi, r, w, hidden, x_row_stride, eps);
   }
+  return launch_rows(rmsnorm_row_regs<T, NPT, false>, rows, threads, stream, o, xi, r, w, hidden, x_row_stride, eps);
 }
 
 template <typename T>
@@ -170,10 +211,10 @@ int launch_typed(void* out, const void* x, void* residual, const void* weight, i
     const int npt = packs <= 128 ? 1 : packs <= 512 ? 2 : packs <= 2048 ? 4 : 8;
     const int threads = std::min(1024, std::max(32, ((packs + npt - 1) / npt + 31) / 32 * 32));
     switch (npt) {
-      case 1: launch_regs<T, 1>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
-      case 2: launch_regs<T, 2>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
-      case 4: launch_regs<T, 4>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
-      default: launch_regs<T, 8>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads); break;
+      case 1: return static_cast<int>(launch_regs<T, 1>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads));
+      case 2: return static_cast<int>(launch_regs<T, 2>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads));
+      case 4: return static_cast<int>(launch_regs<T, 4>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads));
+      default: return static_cast<int>(launch_regs<T, 8>(out, x, residual, weight, rows, hidden, x_row_stride, eps, stream, threads));
     }
   } else {
     const int threads = std::min(1024, std::max(32, (hidden + 31) / 32 * 32));
@@ -182,12 +223,12 @@ int launch_typed(void* out, const void* x, void* residual, const void* weight, i
     auto r = static_cast<T*>(residual);
     auto w = static_cast<const T*>(weight);
     if (residual) {
-      rmsnorm_row_twopass<T, true><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
-    } else {
-      rmsnorm_row_twopass<T, false><<<rows, threads, 0, stream>>>(o, xi, r, w, hidden, x_row_stride, eps);
+      return static_cast<int>(
+          launch_rows(rmsnorm_row_twopass<T, true>, rows, threads, stream, o, xi, r, w, hidden, x_row_stride, eps));
     }
+    return static_cast<int>(
+        launch_rows(rmsnorm_row_twopass<T, false>, rows, threads, stream, o, xi, r, w, hidden, x_row_stride, eps));
   }
-  return static_cast<int>(cudaGetLastError());
 }
 
 }  // namespace
