@@ -1473,9 +1473,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 // through two shared-memory stages, the next chunk's loads in flight during the current chunk's
 // work. Per chunk:
 //   one thread issues S = Q.K^T (M = 128 rows, N = 128 tokens, K = head_dim) into TMEM;
-//   each thread owns one row (one TMEM lane): the chunk's row maximum, the online softmax with a
-//   lazy rescale (O in TMEM is rescaled only when a row's maximum grows by more than 2^8, so the
-//   exponentials stay below 2^8 otherwise), P written to shared memory as the next A operand;
+//   two warpgroups split every row (TMEM lane) by columns, one thread per half row: the chunk's
+//   row maximum (the halves exchange theirs), the online softmax with a lazy rescale (O in TMEM is
+//   rescaled only when a row's maximum grows by more than 2^8, so the exponentials stay below 2^8
+//   otherwise), P written to shared memory as the next A operand;
 //   one thread issues O += P.V (N = head_dim, K = chunk tokens; V as an MN-major operand).
 // tcgen05 operations of one thread complete in issue order, so once S of chunk j has completed,
 // O += P.V of chunk j-1 has too: the rescale and the reuse of its stage need no further wait.
@@ -1483,7 +1484,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 // row's sequence; cascade_prefix_reduce_kernel collapses a prefix's planes.
 
 constexpr int kPrefixTokens = 128;    // tokens of one chunk: the N of S = Q.K^T, the K of O = P.V
-constexpr int kPrefixThreads = 128;   // one thread per query row / TMEM lane
+constexpr int kPrefixThreads = 256;   // two warpgroups: each row's columns split between them
 constexpr int kPrefixChunksMax = 8;   // chunks of one CTA's segment, at most
 constexpr float kLazyRescale = 8.0f;  // log2 headroom before O is rescaled
 
@@ -1519,7 +1520,7 @@ __host__ __device__ inline PrefixLayout prefix_layout(int D) {
   L.bars = off;
   L.tptr = off + 64u;
   L.ints = off + 128u;
-  L.total = L.ints + 512u * 4u + 1024u;  // + slack to align the base to 1024 B
+  L.total = L.ints + 1536u * 4u + 1024u;  // + slack to align the base to 1024 B
   return L;
 }
 
@@ -1568,10 +1569,10 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     }
     if (__syncthreads_or(bad)) return;  // the decode kernel reports it and ignores the prefixes
     ints[tid] = local;
-    if (tid == 0) ints[300] = -1;
+    if (tid == 0) ints[560] = -1;
     __syncthreads();
-    block_scan(kPrefixThreads, [&](int i) { return ints[i]; }, ints + 128, ints + 260);
-    const int first = ints[128 + tid];
+    block_scan(kPrefixThreads, [&](int i) { return ints[i]; }, ints + 256, ints + 520);
+    const int first = ints[256 + tid];
     const int z = blockIdx.z;
     if (z >= first && z < first + local) {
       int acc = first;
@@ -1580,9 +1581,9 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
         const int nb = i1 > i0 ? (i1 - i0 + Mb - 1) / Mb : 0;
         if (z < acc + nb) {
           const int b0 = i0 + (z - acc) * Mb;
-          ints[300] = p;
-          ints[301] = b0;
-          ints[302] = min(Mb, i1 - b0);
+          ints[560] = p;
+          ints[561] = b0;
+          ints[562] = min(Mb, i1 - b0);
           break;
         }
         acc += nb;
@@ -1590,9 +1591,9 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     }
     __syncthreads();
   }
-  const int grp = ints[300];
+  const int grp = ints[560];
   if (grp < 0) return;
-  const int b0 = ints[301], nmem = ints[302];
+  const int b0 = ints[561], nmem = ints[562];
   const int plen = clamp_prefix_len(a, grp, false);
   const int tok_seg = seg * nseg_chunks * CT;
   if (tok_seg >= plen) return;
@@ -1604,9 +1605,9 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
 
   // One parallel round of small loads: the segment's page ids (-1: outside the pool) and the
   // block's sequences' own lengths.
-  int* s_page = ints + 320;  // up to kPrefixChunksMax * CT / 8 = 128 pages: 320..447
-  int* s_own = ints + 192;   // the scan scratch is free again: up to 128 lengths at 192..319
-  __syncthreads();           // every thread has read ints[128 + tid] before 192.. is reused
+  int* s_own = ints + 576;   // up to 128 lengths: 576..703
+  int* s_page = ints + 704;  // up to kPrefixChunksMax * CT / 8 = 128 pages: 704..831
+  float* s_half = reinterpret_cast<float*>(ints + 832);  // [2 halves][128 rows]: chunk max, then row sum
   for (int i = tid; i < npg; i += kPrefixThreads) {
     const int page = __ldg(a.prefix_bt + static_cast<int64_t>(grp) * a.prefix_bt_stride + tok_seg / P + i);
     s_page[i] = (page < 0 || (a.num_pages >= 0 && page >= a.num_pages)) ? -1 : page;
@@ -1678,7 +1679,14 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     issue_chunk(0);
   }
 
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  // Thread tid works on row rw = tid % 128 (TMEM lane; warp w reads lanes 32 * (w % 4) ..) and
+  // on half hf = tid / 128 of that row's columns: S columns hf * CT/2 .., P's 64-token block hf,
+  // O columns hf * D/2 ... The halves share the chunk maximum (so both make the same rescale
+  // decision) and add their row sums at the end.
+  const int rw = tid & 127, hf = tid >> 7;
+  constexpr int SC = CT / 2, OC = D / 2;  // S and O columns per half
+  static_assert(SC == 64, "a half's S columns are one 64-token block of P");
+  const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
   const float sl = a.scale_log2;
   float m_used = -INFINITY, lsum = 0.0f;
   bool ok = true;
@@ -1708,20 +1716,23 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     tcgen05_fence_after();
     if (warp == 0 && j + 1 < nchunk) issue_chunk(j + 1);
 
-    // ---- this thread's row of S: the chunk's maximum, a lazy rescale, P
-    uint32_t sr[CT / 32][32];
+    // ---- this thread's half row of S: the chunk's maximum, a lazy rescale, P
+    uint32_t sr[SC / 32][32];
     __syncwarp();  // tcgen05.ld is .sync.aligned
 #pragma unroll
-    for (int cc = 0; cc < CT / 32; ++cc) tmem_ld32(tS + lane_base + cc * 32, sr[cc]);
+    for (int cc = 0; cc < SC / 32; ++cc) tmem_ld32(tS + lane_base + hf * SC + cc * 32, sr[cc]);
     tmem_wait_ld();
     float mc = -INFINITY;
 #pragma unroll
-    for (int cc = 0; cc < CT / 32; ++cc) {
+    for (int cc = 0; cc < SC / 32; ++cc) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (cc * 32 + i < ntok) mc = fmaxf(mc, __uint_as_float(sr[cc][i]) * sl);
+        if (hf * SC + cc * 32 + i < ntok) mc = fmaxf(mc, __uint_as_float(sr[cc][i]) * sl);
       }
     }
+    s_half[hf * 128 + rw] = mc;
+    __syncthreads();
+    mc = fmaxf(s_half[rw], s_half[128 + rw]);
     float alpha = 1.0f;
     if (mc > m_used + kLazyRescale) {  // also the first chunk, where m_used = -inf
       alpha = m_used == -INFINITY ? 0.0f : fast_exp2(m_used - mc);
@@ -1729,27 +1740,27 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
       lsum *= alpha;
     }
     if (j > 0 && __any_sync(0xffffffffu, alpha < 1.0f)) {
-      // O (complete up to chunk j - 1) *= alpha for this warp's rows, through registers.
+      // O (complete up to chunk j - 1) *= alpha for this warp's rows and half, through registers.
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = 0; cc < OC / 32; ++cc) {
         uint32_t r[32];
-        tmem_ld32(tO + lane_base + cc * 32, r);
+        tmem_ld32(tO + lane_base + hf * OC + cc * 32, r);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-        tmem_st32(tO + lane_base + cc * 32, r);
+        tmem_st32(tO + lane_base + hf * OC + cc * 32, r);
       }
       tmem_wait_st();
     }
     const uint32_t sp = base + L.p[s];
 #pragma unroll
-    for (int cc = 0; cc < CT / 32; ++cc) {
+    for (int cc = 0; cc < SC / 32; ++cc) {
 #pragma unroll
       for (int q8 = 0; q8 < 4; ++q8) {  // 8 tokens: one 16-byte unit of P's row
         uint32_t w[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int t0 = cc * 32 + q8 * 8 + 2 * u;
+          const int t0 = hf * SC + cc * 32 + q8 * 8 + 2 * u;
           const float s0 = __uint_as_float(sr[cc][q8 * 8 + 2 * u]) * sl;
           const float s1 = __uint_as_float(sr[cc][q8 * 8 + 2 * u + 1]) * sl;
           const float p0 = t0 < ntok ? fast_exp2(s0 - m_used) : 0.0f;
@@ -1758,9 +1769,8 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
           const float2 f = Storage<T>::unpack2(w[u]);  // the normaliser sums what the MMA uses
           lsum += f.x + f.y;
         }
-        const int tok = cc * 32 + q8 * 8;
-        const uint32_t unit = static_cast<uint32_t>((tok % 64) / 8) ^ static_cast<uint32_t>(tid & 7);
-        sts128(sp + (tok / 64) * PH + tid * 128u + (unit << 4), make_uint4(w[0], w[1], w[2], w[3]));
+        const uint32_t unit = static_cast<uint32_t>(cc * 4 + q8) ^ static_cast<uint32_t>(rw & 7);
+        sts128(sp + hf * PH + rw * 128u + (unit << 4), make_uint4(w[0], w[1], w[2], w[3]));
       }
     }
     // V rows past the chunk's tokens (a page's tail) are zeroed: P is zero there, but 0 * NaN is not.
@@ -1788,30 +1798,32 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     }
   }
   ok = mbar_wait_bounded(bo, (nchunk - 1) & 1, a.sync, kWaitLimit) && ok;
+  s_half[hf * 128 + rw] = lsum;
   ok = __syncthreads_and(ok);  // one verdict for the CTA (only thread 0 waited on the loads)
+  lsum = s_half[rw] + s_half[128 + rw];  // the two halves' sums, in a fixed order
   tcgen05_fence_after();
 
   // ---- epilogue: row tid = member m, query head gi of KV head kvh. A sequence whose prefix is
   // this one segment and that has no tokens of its own gets its final output here; otherwise the
   // row becomes prefix plane `seg` (collapsed by cascade_prefix_reduce_kernel when the prefix has
   // several, merged with the sequence's own tokens by the decode kernel).
-  const int m = tid / G, gi = tid - m * G;
+  const int m = rw / G, gi = rw - m * G;
   const bool valid = ok && m < nmem;
   const bool direct = valid && nplanes == 1 && s_own[m] == 0;
   const int64_t row = static_cast<int64_t>(b0 + m) * a.num_q_heads + kvh * G + gi;
   const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
   const float lse = lsum > 0.0f ? m_used + __log2f(lsum) : -INFINITY;
-  uint32_t orr[D / 32][32];
+  uint32_t orr[OC / 32][32];
   __syncwarp();  // tcgen05.ld is .sync.aligned
 #pragma unroll
-  for (int cc = 0; cc < D / 32; ++cc) tmem_ld32(tO + lane_base + cc * 32, orr[cc]);
+  for (int cc = 0; cc < OC / 32; ++cc) tmem_ld32(tO + lane_base + hf * OC + cc * 32, orr[cc]);
   tmem_wait_ld();
 #pragma unroll
-  for (int cc = 0; cc < D / 32; ++cc) {
+  for (int cc = 0; cc < OC / 32; ++cc) {
     const uint32_t(&r)[32] = orr[cc];
     if (!valid) continue;
     if (direct) {
-      T* dst = static_cast<T*>(a.out) + row * D + cc * 32;
+      T* dst = static_cast<T*>(a.out) + row * D + hf * OC + cc * 32;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 pk;
@@ -1823,7 +1835,7 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
       }
     } else {
       float4* dst = reinterpret_cast<float4*>(
-          a.cas_o + (static_cast<int64_t>(seg) * B * a.num_q_heads + row) * D + cc * 32);
+          a.cas_o + (static_cast<int64_t>(seg) * B * a.num_q_heads + row) * D + hf * OC + cc * 32);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         dst[q] = make_float4(__uint_as_float(r[4 * q]) * inv, __uint_as_float(r[4 * q + 1]) * inv,
@@ -1831,7 +1843,7 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
       }
     }
   }
-  if (valid && !direct) a.cas_lse[static_cast<int64_t>(seg) * B * a.num_q_heads + row] = lse;
+  if (valid && !direct && hf == 0) a.cas_lse[static_cast<int64_t>(seg) * B * a.num_q_heads + row] = lse;
   tcgen05_fence_before();
   __syncthreads();  // every TMEM read done
   if (warp == 0) {
