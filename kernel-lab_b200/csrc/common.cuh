@@ -104,6 +104,15 @@ enum StatusBits : uint32_t {
   kStatusBadPrefixGroups = 8u,  // cascade groups do not partition the batch: prefixes were ignored
 };
 
+// ----------------------------------------------------------------- programmatic dependent launch
+
+// For kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization: wait until the
+// previous kernel in the stream has completed and its writes are visible (returns at once when it
+// already has, or when this kernel was launched without the attribute); let the next kernel in
+// the stream start launching.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ----------------------------------------------------------------- shared-memory addresses
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

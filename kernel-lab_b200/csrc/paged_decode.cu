@@ -867,6 +867,12 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     tma_prefetch_descriptor(&tmk);
     tma_prefetch_descriptor(&tmv);
   }
+  // Launched with programmatic stream serialization: the prologue above overlaps the previous
+  // kernel's tail; nothing global (inputs, status word, scratch shared with the previous call) is
+  // touched before that kernel has completed. The next call may start launching right away: its
+  // CTAs can only take an SM this grid has left.
+  wait_prior_grid();
+  allow_next_grid();
   plan_build(a, ps);
   volatile int* abort_flag = misc + 2;
 
@@ -2452,12 +2458,24 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 template <typename T, int D, int NT, bool KV8>
 cudaError_t launch_tc_one(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                           cudaStream_t st) {
-  if (p.groups > 0) {
-    decode_tc_kernel<T, D, NT, KV8, true><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-  } else {
-    decode_tc_kernel<T, D, NT, KV8, false><<<p.grid, kTCThreads, p.smem, st>>>(tmk, tmv, a, p.shape);
-  }
-  return cudaGetLastError();
+  // Programmatic stream serialization (KL_DECODE_PDL=0: off, read once): the kernel may begin its
+  // prologue while the previous kernel in the stream finishes (see decode_tc_kernel).
+  static const bool pdl = [] {
+    const char* v = std::getenv("KL_DECODE_PDL");
+    return !(v && std::atoi(v) == 0);
+  }();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid));
+  cfg.blockDim = dim3(kTCThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (p.groups > 0) return cudaLaunchKernelEx(&cfg, decode_tc_kernel<T, D, NT, KV8, true>, tmk, tmv, a, p.shape);
+  return cudaLaunchKernelEx(&cfg, decode_tc_kernel<T, D, NT, KV8, false>, tmk, tmv, a, p.shape);
 }
 
 template <typename T, bool KV8>

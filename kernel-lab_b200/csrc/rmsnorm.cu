@@ -43,11 +43,6 @@ struct Pack16 {
   };
 };
 
-// Programmatic dependent launch: wait for the previous kernel in the stream (no-op when it has
-// finished, or when this kernel was launched without the attribute); let the next one launch.
-__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 // Sum over the block; every thread gets the total. `red` holds one float per warp.
 __device__ __forceinline__ float block_allreduce_sum(float v, float* red) {
   const int lane = threadIdx.x & 31;
