@@ -1561,6 +1561,10 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
   const int seg = blockIdx.x, kvh = blockIdx.y;
   const int nseg_chunks = a.prefix_chunk / CT;  // chunks per segment
 
+  // Launched with programmatic stream serialization: nothing global is touched before the
+  // previous kernel in the stream (possibly the previous call, which shares the prefix planes)
+  // has completed.
+  wait_prior_grid();
   // ---- member block blockIdx.z: its group (a block scan over the groups' block counts)
   {
     const int ngrp = a.num_prefixes;
@@ -1808,6 +1812,7 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
   ok = __syncthreads_and(ok);  // one verdict for the CTA (only thread 0 waited on the loads)
   lsum = s_half[rw] + s_half[128 + rw];  // the two halves' sums, in a fixed order
   tcgen05_fence_after();
+  allow_next_grid();  // the reduce kernel may start launching (it waits for this grid's stores)
 
   // ---- epilogue: row tid = member m, query head gi of KV head kvh. A sequence whose prefix is
   // this one segment and that has no tokens of its own gets its final output here; otherwise the
@@ -1871,6 +1876,7 @@ __global__ void __launch_bounds__(kReduceThreads) cascade_prefix_reduce_kernel(c
   constexpr int Q = D / 4;
   static_assert(32 % Q == 0, "a query row's columns must sit in one warp");
   constexpr int KB = 8;
+  wait_prior_grid();  // the prefix kernel's planes are complete and visible
   const int64_t rows = static_cast<int64_t>(a.batch) * a.num_q_heads;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kReduceThreads + threadIdx.x;
   const int64_t row = min(i / Q, rows - 1);
@@ -2455,27 +2461,40 @@ bool encode_q_map(CUtensorMap* map, const void* q, int dtype, int batch, int Hq,
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-template <typename T, int D, int NT, bool KV8>
-cudaError_t launch_tc_one(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                          cudaStream_t st) {
-  // Programmatic stream serialization (KL_DECODE_PDL=0: off, read once): the kernel may begin its
-  // prologue while the previous kernel in the stream finishes (see decode_tc_kernel).
-  static const bool pdl = [] {
+// Launch with programmatic stream serialization (KL_DECODE_PDL=0: without, read once): the kernel
+// may begin while the previous kernel in the stream finishes; every kernel launched this way calls
+// wait_prior_grid() before touching global memory.
+bool decode_pdl() {
+  static const bool on = [] {
     const char* v = std::getenv("KL_DECODE_PDL");
     return !(v && std::atoi(v) == 0);
   }();
+  return on;
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, int threads, size_t smem, cudaStream_t st,
+                       const Args&... args) {
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.grid));
-  cfg.blockDim = dim3(kTCThreads);
-  cfg.dynamicSmemBytes = p.smem;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  if (p.groups > 0) return cudaLaunchKernelEx(&cfg, decode_tc_kernel<T, D, NT, KV8, true>, tmk, tmv, a, p.shape);
-  return cudaLaunchKernelEx(&cfg, decode_tc_kernel<T, D, NT, KV8, false>, tmk, tmv, a, p.shape);
+  cfg.numAttrs = decode_pdl() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <typename T, int D, int NT, bool KV8>
+cudaError_t launch_tc_one(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                          cudaStream_t st) {
+  // The kernel's prologue may overlap the previous kernel in the stream (see decode_tc_kernel).
+  const dim3 grid(static_cast<unsigned>(p.grid));
+  if (p.groups > 0) return launch_pdl(decode_tc_kernel<T, D, NT, KV8, true>, grid, kTCThreads, p.smem, st, tmk, tmv, a, p.shape);
+  return launch_pdl(decode_tc_kernel<T, D, NT, KV8, false>, grid, kTCThreads, p.smem, st, tmk, tmv, a, p.shape);
 }
 
 template <typename T, bool KV8>
@@ -2593,25 +2612,26 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
       return static_cast<int>(cudaErrorInvalidValue);
     }
     const dim3 grid(p.cas_planes, Hkv, (batch + 128 / G - 1) / (128 / G) + cas.groups);
+    cudaError_t e;
     if (dtype == KL_FLOAT16) {
-      if (D == 64) cascade_prefix_kernel<__half, 64><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
-      else cascade_prefix_kernel<__half, 128><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
+      e = D == 64 ? launch_pdl(cascade_prefix_kernel<__half, 64>, grid, kPrefixThreads, p.prefix_smem, st, tmq, tpk, tpv, a)
+                  : launch_pdl(cascade_prefix_kernel<__half, 128>, grid, kPrefixThreads, p.prefix_smem, st, tmq, tpk, tpv, a);
     } else {
-      if (D == 64) cascade_prefix_kernel<__nv_bfloat16, 64><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
-      else cascade_prefix_kernel<__nv_bfloat16, 128><<<grid, kPrefixThreads, p.prefix_smem, st>>>(tmq, tpk, tpv, a);
+      e = D == 64 ? launch_pdl(cascade_prefix_kernel<__nv_bfloat16, 64>, grid, kPrefixThreads, p.prefix_smem, st, tmq, tpk, tpv, a)
+                  : launch_pdl(cascade_prefix_kernel<__nv_bfloat16, 128>, grid, kPrefixThreads, p.prefix_smem, st, tmq, tpk, tpv, a);
     }
-    if (const cudaError_t e = cudaGetLastError(); e != cudaSuccess) return static_cast<int>(e);
+    if (e != cudaSuccess) return static_cast<int>(e);
     if (p.cas_planes > 1) {
       const int64_t threads = static_cast<int64_t>(batch) * Hq * (D / 4);  // one per float4 column
-      const unsigned blocks = static_cast<unsigned>((threads + kReduceThreads - 1) / kReduceThreads);
+      const dim3 blocks(static_cast<unsigned>((threads + kReduceThreads - 1) / kReduceThreads));
       if (dtype == KL_FLOAT16) {
-        if (D == 64) cascade_prefix_reduce_kernel<__half, 64><<<blocks, kReduceThreads, 0, st>>>(a);
-        else cascade_prefix_reduce_kernel<__half, 128><<<blocks, kReduceThreads, 0, st>>>(a);
+        e = D == 64 ? launch_pdl(cascade_prefix_reduce_kernel<__half, 64>, blocks, kReduceThreads, 0, st, a)
+                    : launch_pdl(cascade_prefix_reduce_kernel<__half, 128>, blocks, kReduceThreads, 0, st, a);
       } else {
-        if (D == 64) cascade_prefix_reduce_kernel<__nv_bfloat16, 64><<<blocks, kReduceThreads, 0, st>>>(a);
-        else cascade_prefix_reduce_kernel<__nv_bfloat16, 128><<<blocks, kReduceThreads, 0, st>>>(a);
+        e = D == 64 ? launch_pdl(cascade_prefix_reduce_kernel<__nv_bfloat16, 64>, blocks, kReduceThreads, 0, st, a)
+                    : launch_pdl(cascade_prefix_reduce_kernel<__nv_bfloat16, 128>, blocks, kReduceThreads, 0, st, a);
       }
-      if (const cudaError_t e = cudaGetLastError(); e != cudaSuccess) return static_cast<int>(e);
+      if (e != cudaSuccess) return static_cast<int>(e);
     }
   }
 
