@@ -8,7 +8,9 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
 
+#include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -112,6 +114,30 @@ enum StatusBits : uint32_t {
 // the stream start launching.
 __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// An on/off switch read from the environment: unset or anything but "0" is on.
+inline bool env_switch_on(const char* name) {
+  const char* v = std::getenv(name);
+  return !(v && std::atoi(v) == 0);
+}
+
+// Host side: launch `kernel` on `st`, with programmatic stream serialization when `pdl` is set.
+// A kernel launched this way must call wait_prior_grid() before it touches global memory.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_kernel(bool pdl, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, const Args&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 // ----------------------------------------------------------------- shared-memory addresses
 

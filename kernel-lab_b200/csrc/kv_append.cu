@@ -43,6 +43,8 @@ struct AppendArgs {
 
 // 16-byte path: every row start and the row length are 16-byte aligned.
 __global__ void __launch_bounds__(kAppendThreads) kv_append_vec16(const AppendArgs a) {
+  wait_prior_grid();
+  allow_next_grid();
   const int b = blockIdx.x;
   const int pos = a.positions[b];
   if (pos < 0) return;
@@ -72,6 +74,8 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_vec16(const AppendAr
 // Element path for anything else (odd head_dim, misaligned views).
 template <typename E>
 __global__ void __launch_bounds__(kAppendThreads) kv_append_scalar(const AppendArgs a) {
+  wait_prior_grid();
+  allow_next_grid();
   const int b = blockIdx.x;
   const int pos = a.positions[b];
   if (pos < 0) return;
@@ -98,6 +102,8 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_scalar(const AppendA
 template <typename E>
 __global__ void __launch_bounds__(kAppendThreads) kv_append_e4m3(const AppendArgs a, const float* k_scale,
                                                                   const float* v_scale, int head_dim) {
+  wait_prior_grid();
+  allow_next_grid();
   const int b = blockIdx.x;
   const int pos = a.positions[b];
   if (pos < 0) return;
@@ -124,6 +130,20 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_e4m3(const AppendArg
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launched with programmatic stream serialization (KL_APPEND_PDL=0: without, read once). Each
+// block waits for the previous kernel before its first global access and at once lets the next
+// kernel (normally the decode that reads these rows, which waits for this grid's completion
+// before its own first global access) start launching into the SMs beside it.
+bool append_pdl() {
+  static const bool on = env_switch_on("KL_APPEND_PDL");
+  return on;
+}
+
+template <typename... Params, typename... Args>
+cudaError_t launch_rows(void (*kernel)(Params...), int batch, cudaStream_t st, const Args&... args) {
+  return launch_kernel(append_pdl(), kernel, dim3(static_cast<unsigned>(batch)), dim3(kAppendThreads), 0, st, args...);
+}
 
 }  // namespace
 }  // namespace klb
@@ -162,14 +182,15 @@ extern "C" int kl_paged_kv_append(int dtype, void* k_cache, void* v_cache, const
   const int64_t row_bytes = row_elems * a.elem_bytes;
   const bool vec = row_bytes % 16 == 0 && (new_row_stride * a.elem_bytes) % 16 == 0 && aligned16(k_cache) &&
                    aligned16(v_cache) && aligned16(k_new) && aligned16(v_new);
+  cudaError_t e;
   if (vec) {
-    kv_append_vec16<<<batch, kAppendThreads, 0, st>>>(a);
+    e = launch_rows(kv_append_vec16, batch, st, a);
   } else if (a.elem_bytes == 4) {
-    kv_append_scalar<float><<<batch, kAppendThreads, 0, st>>>(a);
+    e = launch_rows(kv_append_scalar<float>, batch, st, a);
   } else {
-    kv_append_scalar<uint16_t><<<batch, kAppendThreads, 0, st>>>(a);
+    e = launch_rows(kv_append_scalar<uint16_t>, batch, st, a);
   }
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(e);
 }
 
 extern "C" int kl_paged_kv_append_fp8(int dtype, void* k_cache, void* v_cache, const void* k_new, const void* v_new,
@@ -203,10 +224,11 @@ extern "C" int kl_paged_kv_append_fp8(int dtype, void* k_cache, void* v_cache, c
   a.elem_bytes = 1;
   a.status = status;
   const auto st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
   switch (dtype) {
-    case KL_FLOAT32: kv_append_e4m3<float><<<batch, kAppendThreads, 0, st>>>(a, k_scale, v_scale, head_dim); break;
-    case KL_FLOAT16: kv_append_e4m3<__half><<<batch, kAppendThreads, 0, st>>>(a, k_scale, v_scale, head_dim); break;
-    default: kv_append_e4m3<__nv_bfloat16><<<batch, kAppendThreads, 0, st>>>(a, k_scale, v_scale, head_dim); break;
+    case KL_FLOAT32: e = launch_rows(kv_append_e4m3<float>, batch, st, a, k_scale, v_scale, head_dim); break;
+    case KL_FLOAT16: e = launch_rows(kv_append_e4m3<__half>, batch, st, a, k_scale, v_scale, head_dim); break;
+    default: e = launch_rows(kv_append_e4m3<__nv_bfloat16>, batch, st, a, k_scale, v_scale, head_dim); break;
   }
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(e);
 }

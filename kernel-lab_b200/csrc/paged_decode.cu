@@ -2465,27 +2465,14 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 // may begin while the previous kernel in the stream finishes; every kernel launched this way calls
 // wait_prior_grid() before touching global memory.
 bool decode_pdl() {
-  static const bool on = [] {
-    const char* v = std::getenv("KL_DECODE_PDL");
-    return !(v && std::atoi(v) == 0);
-  }();
+  static const bool on = env_switch_on("KL_DECODE_PDL");
   return on;
 }
 
 template <typename... Params, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, int threads, size_t smem, cudaStream_t st,
                        const Args&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(static_cast<unsigned>(threads));
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = decode_pdl() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kernel, args...);
+  return launch_kernel(decode_pdl(), kernel, grid, dim3(static_cast<unsigned>(threads)), smem, st, args...);
 }
 
 template <typename T, int D, int NT, bool KV8>

@@ -157,27 +157,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // KL_RMSNORM_PDL=0 launches without programmatic stream serialization (read once).
 bool use_pdl() {
-  static const bool on = [] {
-    const char* v = std::getenv("KL_RMSNORM_PDL");
-    return !(v && std::atoi(v) == 0);
-  }();
+  static const bool on = env_switch_on("KL_RMSNORM_PDL");
   return on;
 }
 
 // One CTA per row, `threads` threads, on `stream`, with programmatic stream serialization.
 template <typename... Params, typename... Args>
 cudaError_t launch_rows(void (*kernel)(Params...), int rows, int threads, cudaStream_t stream, Args... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(rows));
-  cfg.blockDim = dim3(static_cast<unsigned>(threads));
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = use_pdl() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+  return launch_kernel(use_pdl(), kernel, dim3(static_cast<unsigned>(rows)), dim3(static_cast<unsigned>(threads)), 0,
+                       stream, static_cast<Params>(args)...);
 }
 
 template <typename T, int NPT>
