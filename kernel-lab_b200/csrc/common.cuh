@@ -61,10 +61,18 @@ struct alignas(sizeof(T) * N) Vec {
   T v[N];
 };
 
-// Two e4m3 values (low byte first) -> f16x2 (low half first); exact, e4m3 being a subset of f16.
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xffffu), __NV_E4M3);
-  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+// Two e4m3 values -> f16x2 (low half first); exact, e4m3 being a subset of f16. The pair is the
+// low (e4m3x2_lo_to_f16x2) or high (e4m3x2_hi_to_f16x2) 16 bits of a word, low byte first; the
+// half is taken as a register half, with no mask or shift.
+__device__ __forceinline__ uint32_t e4m3x2_lo_to_f16x2(uint32_t word) {
+  uint32_t r;
+  asm("{\n.reg .b16 lo, hi;\nmov.b32 {lo, hi}, %1;\ncvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(r) : "r"(word));
+  return r;
+}
+__device__ __forceinline__ uint32_t e4m3x2_hi_to_f16x2(uint32_t word) {
+  uint32_t r;
+  asm("{\n.reg .b16 lo, hi;\nmov.b32 {lo, hi}, %1;\ncvt.rn.f16x2.e4m3x2 %0, hi;\n}" : "=r"(r) : "r"(word));
+  return r;
 }
 
 // A packed pair of the storage type -> f16x2 (the operand type of the fp8-cache MMAs).

@@ -1117,8 +1117,8 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
             const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
-              const uint32_t a0 = e4m3x2_to_f16x2(xw[jj]), a2 = e4m3x2_to_f16x2(xw[jj] >> 16);
-              const uint32_t a1 = e4m3x2_to_f16x2(yw[jj]), a3 = e4m3x2_to_f16x2(yw[jj] >> 16);
+              const uint32_t a0 = e4m3x2_lo_to_f16x2(xw[jj]), a2 = e4m3x2_hi_to_f16x2(xw[jj]);
+              const uint32_t a1 = e4m3x2_lo_to_f16x2(yw[jj]), a3 = e4m3x2_hi_to_f16x2(yw[jj]);
               const int j = 8 * c + 4 * par + jj;
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(sc[nt], a0, a1, a2, a3, qf[j][nt][0], qf[j][nt][1]);
@@ -1198,10 +1198,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
             const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
             const uint32_t x01 = __byte_perm(va[mt >> 1], vb[mt >> 1], sel);
             const uint32_t x23 = __byte_perm(vc[mt >> 1], vd[mt >> 1], sel);
-            a0 = e4m3x2_to_f16x2(x01);
-            a1 = e4m3x2_to_f16x2(x01 >> 16);
-            a2 = e4m3x2_to_f16x2(x23);
-            a3 = e4m3x2_to_f16x2(x23 >> 16);
+            a0 = e4m3x2_lo_to_f16x2(x01);
+            a1 = e4m3x2_hi_to_f16x2(x01);
+            a2 = e4m3x2_lo_to_f16x2(x23);
+            a3 = e4m3x2_hi_to_f16x2(x23);
           }
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
