@@ -1092,10 +1092,31 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       const uint32_t sk = ring + stage * L.stage_bytes;
       const uint32_t sv = sk + L.half;
 
-      // S = K . Q^T : [16 tokens x 8 heads] per n-tile.
-      float sc[NT][4];
+      // V rows of this tile for piece c: tokens 2t4, 2t4+1, 2t4+8, 2t4+9 (zero past the valid ones).
+      auto load_v = [&](int c, uint4 (&v)[4]) {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int tok = 2 * t4 + (q4 & 1) + 8 * (q4 >> 1);
+          const int r = stage_row(tok, ht * NCH + c);
+          v[q4] = lds128(sv + r * 128 + ((g ^ (r & 7)) << 4));
+          if (tok >= valid) v[q4] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      };
+      // e4m3 with one piece (outside a cascade, whose kernel has no registers to spare): the V
+      // rows are read before the score product, so their shared-memory latency overlaps the
+      // MMAs and the softmax instead of following them, and the score product sums its k-steps
+      // into two accumulators (even and odd), halving its chain of dependent MMAs.
+      constexpr bool kEarlyV = KV8 && NCH == 1 && !CAS;
+      uint4 v_early[4];
+      if constexpr (kEarlyV) load_v(0, v_early);
+
+      // S = K . Q^T : [16 tokens x 8 heads] per n-tile.
+      float sc[NT][4], sc_odd[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] = sc_odd[nt][e] = 0.0f;
+      }
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         const int ra = stage_row(g, ht * NCH + c);      // token g
@@ -1121,9 +1142,18 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
               const uint32_t a1 = e4m3x2_lo_to_f16x2(yw[jj]), a3 = e4m3x2_hi_to_f16x2(yw[jj]);
               const int j = 8 * c + 4 * par + jj;
 #pragma unroll
-              for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(sc[nt], a0, a1, a2, a3, qf[j][nt][0], qf[j][nt][1]);
+              for (int nt = 0; nt < NT; ++nt) {
+                Mma<MT>::run((kEarlyV && (jj & 1)) ? sc_odd[nt] : sc[nt], a0, a1, a2, a3, qf[j][nt][0], qf[j][nt][1]);
+              }
             }
           }
+        }
+      }
+      if constexpr (kEarlyV) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[nt][e] += sc_odd[nt][e];
         }
       }
 
@@ -1171,12 +1201,11 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         uint4 v[4];
+        if constexpr (kEarlyV) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int tok = 2 * t4 + (q4 & 1) + 8 * (q4 >> 1);  // 2t4, 2t4+1, 2t4+8, 2t4+9
-          const int r = stage_row(tok, ht * NCH + c);
-          v[q4] = lds128(sv + r * 128 + ((g ^ (r & 7)) << 4));
-          if (tok >= valid) v[q4] = make_uint4(0u, 0u, 0u, 0u);
+          for (int q4 = 0; q4 < 4; ++q4) v[q4] = v_early[q4];
+        } else {
+          load_v(c, v);
         }
         const uint32_t va[4] = {v[0].x, v[0].y, v[0].z, v[0].w};
         const uint32_t vb[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
