@@ -1107,6 +1107,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       // MMAs and the softmax instead of following them, and the score product sums its k-steps
       // into two accumulators (even and odd), halving its chain of dependent MMAs.
       constexpr bool kEarlyV = KV8 && NCH == 1 && !CAS;
+      // The 16-bit kernel splits its score chain the same way where it has registers to spare
+      // (one n-tile, head_dim <= 128, outside a cascade).
+      constexpr bool kTwoAcc = kEarlyV || (!KV8 && !CAS && NT == 1 && D <= 128);
       uint4 v_early[4];
       if constexpr (kEarlyV) load_v(0, v_early);
 
@@ -1131,7 +1134,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
               Mma<MT>::run(sc[nt], x.x, y.x, x.y, y.y, qf[j0][nt][0], qf[j0][nt][1]);
-              Mma<MT>::run(sc[nt], x.z, y.z, x.w, y.w, qf[j0 + 1][nt][0], qf[j0 + 1][nt][1]);
+              Mma<MT>::run(kTwoAcc ? sc_odd[nt] : sc[nt], x.z, y.z, x.w, y.w, qf[j0 + 1][nt][0], qf[j0 + 1][nt][1]);
             }
           } else {
             // 16 e4m3 of d = 128c + 64par + 16t4 + 4jj + {0,1 | 2,3} feed k-step 8c + 4par + jj.
@@ -1143,13 +1146,13 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
               const int j = 8 * c + 4 * par + jj;
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
-                Mma<MT>::run((kEarlyV && (jj & 1)) ? sc_odd[nt] : sc[nt], a0, a1, a2, a3, qf[j][nt][0], qf[j][nt][1]);
+                Mma<MT>::run((kTwoAcc && (jj & 1)) ? sc_odd[nt] : sc[nt], a0, a1, a2, a3, qf[j][nt][0], qf[j][nt][1]);
               }
             }
           }
         }
       }
-      if constexpr (kEarlyV) {
+      if constexpr (kTwoAcc) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
