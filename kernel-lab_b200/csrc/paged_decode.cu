@@ -1764,14 +1764,22 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
 #pragma unroll
     for (int cc = 0; cc < SC / 32; ++cc) tmem_ld32(tS + lane_base + hf * SC + cc * 32, sr[cc]);
     tmem_wait_ld();
-    float mc = -INFINITY;
+    // Every chunk but a prefix's last is full: its softmax runs without the per-column masks.
+    // The operations are the same; the compiler may fuse a multiply and a subtraction
+    // differently in the two bodies, so the outputs can differ in the last bit.
+    const bool full = ntok == CT;
+    auto half_max = [&](auto all_valid) {
+      float m = -INFINITY;
 #pragma unroll
-    for (int cc = 0; cc < SC / 32; ++cc) {
+      for (int cc = 0; cc < SC / 32; ++cc) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (hf * SC + cc * 32 + i < ntok) mc = fmaxf(mc, __uint_as_float(sr[cc][i]) * sl);
+        for (int i = 0; i < 32; ++i) {
+          if (decltype(all_valid)::value || hf * SC + cc * 32 + i < ntok) m = fmaxf(m, __uint_as_float(sr[cc][i]) * sl);
+        }
       }
-    }
+      return m;
+    };
+    float mc = full ? half_max(std::true_type{}) : half_max(std::false_type{});
     s_half[hf * 128 + rw] = mc;
     __syncthreads();
     mc = fmaxf(s_half[rw], s_half[128 + rw]);
@@ -1795,25 +1803,33 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
       tmem_wait_st();
     }
     const uint32_t sp = base + L.p[s];
+    auto write_p = [&](auto all_valid) {
+      constexpr bool kAll = decltype(all_valid)::value;
 #pragma unroll
-    for (int cc = 0; cc < SC / 32; ++cc) {
+      for (int cc = 0; cc < SC / 32; ++cc) {
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {  // 8 tokens: one 16-byte unit of P's row
-        uint32_t w[4];
+        for (int q8 = 0; q8 < 4; ++q8) {  // 8 tokens: one 16-byte unit of P's row
+          uint32_t w[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int t0 = hf * SC + cc * 32 + q8 * 8 + 2 * u;
-          const float s0 = __uint_as_float(sr[cc][q8 * 8 + 2 * u]) * sl;
-          const float s1 = __uint_as_float(sr[cc][q8 * 8 + 2 * u + 1]) * sl;
-          const float p0 = t0 < ntok ? fast_exp2(s0 - m_used) : 0.0f;
-          const float p1 = t0 + 1 < ntok ? fast_exp2(s1 - m_used) : 0.0f;
-          w[u] = Storage<T>::pack2(p0, p1);
-          const float2 f = Storage<T>::unpack2(w[u]);  // the normaliser sums what the MMA uses
-          lsum += f.x + f.y;
+          for (int u = 0; u < 4; ++u) {
+            const int t0 = hf * SC + cc * 32 + q8 * 8 + 2 * u;
+            const float s0 = __uint_as_float(sr[cc][q8 * 8 + 2 * u]) * sl;
+            const float s1 = __uint_as_float(sr[cc][q8 * 8 + 2 * u + 1]) * sl;
+            const float p0 = (kAll || t0 < ntok) ? fast_exp2(s0 - m_used) : 0.0f;
+            const float p1 = (kAll || t0 + 1 < ntok) ? fast_exp2(s1 - m_used) : 0.0f;
+            w[u] = Storage<T>::pack2(p0, p1);
+            const float2 f = Storage<T>::unpack2(w[u]);  // the normaliser sums what the MMA uses
+            lsum += f.x + f.y;
+          }
+          const uint32_t unit = static_cast<uint32_t>(cc * 4 + q8) ^ static_cast<uint32_t>(rw & 7);
+          sts128(sp + hf * PH + rw * 128u + (unit << 4), make_uint4(w[0], w[1], w[2], w[3]));
         }
-        const uint32_t unit = static_cast<uint32_t>(cc * 4 + q8) ^ static_cast<uint32_t>(rw & 7);
-        sts128(sp + hf * PH + rw * 128u + (unit << 4), make_uint4(w[0], w[1], w[2], w[3]));
       }
+    };
+    if (full) {
+      write_p(std::true_type{});
+    } else {
+      write_p(std::false_type{});
     }
     // V rows past the chunk's tokens (a page's tail) are zeroed: P is zero there, but 0 * NaN is not.
     ok = mbar_wait_bounded(bv(s), (j >> 1) & 1, a.sync, kWaitLimit) && ok;
