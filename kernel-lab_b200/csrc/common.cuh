@@ -75,6 +75,23 @@ __device__ __forceinline__ uint32_t e4m3x2_hi_to_f16x2(uint32_t word) {
   return r;
 }
 
+// lo += the low element, hi += the high element of a packed 16-bit pair, each widened exactly and
+// added with one mixed-precision add (no unpacking into two floats first).
+template <typename T>
+__device__ __forceinline__ void add_pair_to(uint32_t w, float& lo, float& hi);
+template <>
+__device__ __forceinline__ void add_pair_to<__nv_bfloat16>(uint32_t w, float& lo, float& hi) {
+  asm("{\n.reg .b16 l, h;\nmov.b32 {l, h}, %2;\nadd.rn.f32.bf16 %0, l, %0;\nadd.rn.f32.bf16 %1, h, %1;\n}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(w));
+}
+template <>
+__device__ __forceinline__ void add_pair_to<__half>(uint32_t w, float& lo, float& hi) {
+  asm("{\n.reg .b16 l, h;\nmov.b32 {l, h}, %2;\nadd.rn.f32.f16 %0, l, %0;\nadd.rn.f32.f16 %1, h, %1;\n}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(w));
+}
+
 // A packed pair of the storage type -> f16x2 (the operand type of the fp8-cache MMAs).
 template <typename T>
 __device__ __forceinline__ uint32_t to_f16x2(uint32_t v);

@@ -1805,6 +1805,7 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     const uint32_t sp = base + L.p[s];
     auto write_p = [&](auto all_valid) {
       constexpr bool kAll = decltype(all_valid)::value;
+      float l_even = 0.0f, l_odd = 0.0f;  // the chunk's even and odd columns, summed apart
 #pragma unroll
       for (int cc = 0; cc < SC / 32; ++cc) {
 #pragma unroll
@@ -1818,13 +1819,13 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
             const float p0 = (kAll || t0 < ntok) ? fast_exp2(s0 - m_used) : 0.0f;
             const float p1 = (kAll || t0 + 1 < ntok) ? fast_exp2(s1 - m_used) : 0.0f;
             w[u] = Storage<T>::pack2(p0, p1);
-            const float2 f = Storage<T>::unpack2(w[u]);  // the normaliser sums what the MMA uses
-            lsum += f.x + f.y;
+            add_pair_to<T>(w[u], l_even, l_odd);  // the normaliser sums what the MMA uses
           }
           const uint32_t unit = static_cast<uint32_t>(cc * 4 + q8) ^ static_cast<uint32_t>(rw & 7);
           sts128(sp + hf * PH + rw * 128u + (unit << 4), make_uint4(w[0], w[1], w[2], w[3]));
         }
       }
+      lsum += l_even + l_odd;
     };
     if (full) {
       write_p(std::true_type{});
