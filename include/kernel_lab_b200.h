@@ -123,25 +123,39 @@ int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* s
  * reserved every free byte for the KV cache, or a step loop that must never call
  * cudaMalloc. It allocates nothing; the caller passes inputs and outputs only. Scratch is
  * one fixed array in this library's device memory, KL_NOALLOC_SCRATCH_BYTES per GPU
- * (16 MiB of split partials + 256 KiB of counters), held from library load until process
- * exit.
+ * (16 MiB of split partials + 256 KiB of counters), held until process exit.
  *
+ * - CUDA reserves the array on a GPU when it loads this library's device code there. With
+ *   lazy module loading (CUDA's default) that is the first kernel launch or symbol lookup on
+ *   that GPU, not dlopen. A host that hands all free memory to its own pools at start-up must
+ *   therefore make one call (or any kl_* launch) on each GPU first, or run with
+ *   CUDA_MODULE_LOADING=EAGER; otherwise that first call can fail with an out-of-memory error.
  * - A problem whose scratch (kl_paged_decode_workspace_size) exceeds that array is rejected
  *   with cudaErrorMemoryAllocation before anything is launched (batch 64, context 4096,
  *   32/8 heads of 128 fit with room to spare).
  * - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
  *   with that device current; make that first call before capturing any stream.
  * - Every call on a device shares the one array and leaves its contents behind; each call
- *   zeroes the counters it needs (a cudaMemsetAsync on `stream`) before its kernel. Calls
- *   that overlap on the GPU (other streams, other host threads) race on the array: run
- *   them in one stream order.
- * Arguments and results are those of kl_paged_decode without the scratch buffers.
+ *   zeroes the counters and the status word (a cudaMemsetAsync on `stream`) before its
+ *   kernel. Calls that overlap on the GPU (other streams, other host threads) race on the
+ *   array: run them in one stream order.
+ * - The status bits of kl_paged_decode (KL_STATUS_*) go to word 0 of the array; read them with
+ *   kl_paged_decode_noalloc_read_status before the next call on the device clears them.
+ * Arguments and results are otherwise those of kl_paged_decode without the scratch buffers.
  * No counterpart in kernel-lab.
  */
 int kl_paged_decode_noalloc(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
                             const int32_t* block_table, const int32_t* seq_lens, int batch, int num_q_heads,
                             int num_kv_heads, int head_dim, int page_size, int64_t block_table_stride,
                             int max_pages_per_seq, int64_t num_pages, float scale, int num_splits, void* stream);
+
+/*
+ * Status bits (KL_STATUS_*) left by the last kl_paged_decode_noalloc call on the current device:
+ * synchronises `stream`, copies word 0 of the library's array to *status and, if clear != 0,
+ * resets it. Call it after the decode and before the next kl_paged_decode_noalloc on this
+ * device, which clears the word. Allocates nothing. No counterpart in kernel-lab.
+ */
+int kl_paged_decode_noalloc_read_status(uint32_t* status, int clear, void* stream);
 
 /*
  * Paged KV append: write each sequence's new token's K and V rows into its pages.

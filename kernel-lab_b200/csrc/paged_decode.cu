@@ -2553,6 +2553,32 @@ cudaError_t launch_tc(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& 
   return p.kv8 ? launch_tc_kind<T, true>(p, tmk, tmv, a, st) : launch_tc_kind<T, false>(p, tmk, tmv, a, st);
 }
 
+// The kernel one call takes, and its plan: the tensor-core kernel where the shape allows it, the
+// buffers are aligned for it (16-byte caches for TMA, q and out for vector loads and stores), TMA
+// row coordinates fit in int32 and both tensor maps encode; otherwise the generic kernel, which
+// has no e4m3 or cascade form (those calls get cudaErrorInvalidValue). On success *use_tc says
+// which, and for the tensor-core kernel *tmk / *tmv hold the caches' tensor maps. Every entry
+// point that launches a decode, or sizes scratch for one it will launch, decides here.
+int choose_kernel(int dtype, const void* out, const void* q, const void* k_cache, const void* v_cache, int batch,
+                  int Hq, int Hkv, int D, int P, int max_pages, int64_t num_pages, int num_splits, bool kv8,
+                  const CascadeIn& cas, Plan& p, CUtensorMap* tmk, CUtensorMap* tmv, bool* use_tc) {
+  *use_tc = false;
+  if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p, kv8, cas.groups,
+                               cas.max_pages)) {
+    return rc;
+  }
+  const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 16) && aligned(out, 16) &&
+                     (num_pages < 0 || num_pages * P <= INT_MAX);
+  if (tc_ok) {
+    const int64_t pool_tokens = num_pages >= 0 ? std::max<int64_t>(num_pages, 1) * P : (int64_t(1) << 31) - 1;
+    *use_tc = encode_kv_map(tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8) &&
+              encode_kv_map(tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8);
+  }
+  if ((kv8 || cas.groups > 0) && !*use_tc) return static_cast<int>(cudaErrorInvalidValue);
+  if (!*use_tc && p.tc) return make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, true, p);
+  return 0;
+}
+
 // k_scale / v_scale non-null: the caches hold e4m3 (tensor-core kernel only, no fallback).
 int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const void* v_cache,
                 const int32_t* block_table, const int32_t* seq_lens, int batch, int Hq, int Hkv, int D, int P,
@@ -2572,24 +2598,11 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   if (kv8 && (!k_scale || !v_scale)) return static_cast<int>(cudaErrorInvalidValue);
   if (bt_stride < 0 || (batch > 1 && bt_stride < max_pages)) return static_cast<int>(cudaErrorInvalidValue);
   Plan p;
-  if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p, kv8, cas.groups,
-                               cas.max_pages)) {
-    return rc;
-  }
-  // The tensor-core path needs 16-byte aligned caches (TMA), q and out (vector loads and
-  // stores) and TMA row coordinates that fit in int32; otherwise take the generic kernel.
-  const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 16) && aligned(out, 16) &&
-                     (num_pages < 0 || num_pages * P <= INT_MAX);
   CUtensorMap tmk, tmv;
   bool use_tc = false;
-  if (tc_ok) {
-    const int64_t pool_tokens = num_pages >= 0 ? std::max<int64_t>(num_pages, 1) * P : (int64_t(1) << 31) - 1;
-    use_tc = encode_kv_map(&tmk, k_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8) &&
-             encode_kv_map(&tmv, v_cache, dtype, pool_tokens, Hkv, D, p.shape.ht, p.shape.p_rows, kv8);
-  }
-  if ((kv8 || cascade) && !use_tc) return static_cast<int>(cudaErrorInvalidValue);  // no generic e4m3 / cascade kernel
-  if (!use_tc && p.tc) {
-    if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, true, p)) return rc;
+  if (const int rc = choose_kernel(dtype, out, q, k_cache, v_cache, batch, Hq, Hkv, D, P, max_pages, num_pages,
+                                   num_splits, kv8, cas, p, &tmk, &tmv, &use_tc)) {
+    return rc;
   }
   if (partial_bytes < p.part_bytes || sync_bytes < p.sync_bytes || !partials) {
     return static_cast<int>(cudaErrorInvalidValue);
@@ -2831,8 +2844,10 @@ int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* s
 // cannot allocate device memory at call time: an inference server whose memory is carved
 // up and owned by its pool at start-up, a runtime that has already reserved every free
 // byte for the KV cache, or code that must not call cudaMalloc (or wait on the caching
-// allocator) from inside its step loop. The scratch is one fixed array per GPU, allocated
-// when the library is loaded and held until the process exits.
+// allocator) from inside its step loop. The scratch is one fixed array per GPU. CUDA reserves
+// it when this library's device code is loaded on that GPU (with lazy module loading, the
+// default, at the first launch or symbol lookup there, not at dlopen) and holds it until the
+// process exits.
 
 namespace klb {
 namespace {
@@ -2872,20 +2887,15 @@ extern "C" int kl_paged_decode_noalloc(int dtype, void* out, const void* q, cons
                                        int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages,
                                        float scale, int num_splits, void* stream) {
   if (batch == 0) return 0;
-  // Size the scratch of the kernel kl_paged_decode will pick for these pointers: the
-  // tensor-core plan when it applies and the buffers are aligned for it, else the generic one.
+  // Size the scratch of the kernel kl_paged_decode will launch for these pointers: the same
+  // choice (tensor-core or generic kernel, tensor maps included) that the launch makes.
   klb::Plan plan;
-  if (const int rc = klb::make_plan(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size,
-                                    max_pages_per_seq, num_splits, false, plan)) {
+  CUtensorMap tmk, tmv;
+  bool use_tc = false;
+  if (const int rc = klb::choose_kernel(dtype, out, q, k_cache, v_cache, batch, num_q_heads, num_kv_heads, head_dim,
+                                        page_size, max_pages_per_seq, num_pages, num_splits, false, klb::CascadeIn{},
+                                        plan, &tmk, &tmv, &use_tc)) {
     return rc;
-  }
-  const bool tc_io = klb::aligned(k_cache, 16) && klb::aligned(v_cache, 16) && klb::aligned(q, 16) &&
-                     klb::aligned(out, 16) && (num_pages < 0 || num_pages * page_size <= INT_MAX);
-  if (plan.tc && !tc_io) {
-    if (const int rc = klb::make_plan(dtype, batch, num_q_heads, num_kv_heads, head_dim, page_size,
-                                      max_pages_per_seq, num_splits, true, plan)) {
-      return rc;
-    }
   }
   const size_t sync_bytes = plan.sync_bytes;
   if (plan.part_bytes > klb::kNoAllocPartialBytes || sync_bytes > klb::kNoAllocSyncBytes) {
@@ -2901,4 +2911,11 @@ extern "C" int kl_paged_decode_noalloc(int dtype, void* out, const void* q, cons
   return kl_paged_decode(dtype, out, q, k_cache, v_cache, block_table, seq_lens, batch, num_q_heads, num_kv_heads,
                          head_dim, page_size, block_table_stride, max_pages_per_seq, num_pages, scale, num_splits,
                          partials, klb::kNoAllocPartialBytes, sync, klb::kNoAllocSyncBytes, stream);
+}
+
+extern "C" int kl_paged_decode_noalloc_read_status(uint32_t* status, int clear, void* stream) {
+  if (!status) return static_cast<int>(cudaErrorInvalidValue);
+  void* base = nullptr;
+  if (const cudaError_t e = klb::noalloc_scratch(&base)) return static_cast<int>(e);
+  return kl_paged_decode_read_status(static_cast<uint8_t*>(base) + klb::kNoAllocPartialBytes, status, clear, stream);
 }

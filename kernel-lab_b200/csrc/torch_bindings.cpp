@@ -15,6 +15,8 @@
 // Decode scratch (split partials and arrival counters) is owned here, one pair of
 // buffers per (device, stream), allocated through PyTorch's caching allocator and grown
 // on demand. The counters are zeroed once at allocation; every call leaves them zero.
+// Entries live as long as the process (a stream that is destroyed keeps its entry, so a
+// host that creates streams per request should reuse a pool of them).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -96,7 +98,11 @@ Scratch& scratch_for(const at::Device& dev, cudaStream_t stream, size_t partial_
     s.partials = at::empty({static_cast<int64_t>(std::max<size_t>(partial_bytes, 256) * 5 / 4)}, opts);
   }
   if (!s.sync.defined() || static_cast<size_t>(s.sync.numel()) < sync_bytes) {
-    s.sync = at::zeros({static_cast<int64_t>(std::max<size_t>(sync_bytes, 256) * 5 / 4)}, opts);
+    at::Tensor grown = at::zeros({static_cast<int64_t>(std::max<size_t>(sync_bytes, 256) * 5 / 4)}, opts);
+    // Status word 0 is sticky until decode_status(clear=True): carry it into the larger buffer
+    // (stream-ordered after every earlier call on this stream; the counters are zero at rest).
+    if (s.sync.defined()) grown.narrow(0, 0, 4).copy_(s.sync.narrow(0, 0, 4), /*non_blocking=*/true);
+    s.sync = grown;
   }
   return s;
 }

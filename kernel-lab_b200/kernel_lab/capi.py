@@ -73,6 +73,7 @@ SIGNATURES = {
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int,
          _c_i64, _c_float, _c_int, _c_vp],
     ),
+    "kl_paged_decode_noalloc_read_status": (_c_int, [_c_u32p, _c_int, _c_vp]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -37,6 +37,7 @@ def test_header_declares_the_abi():
         "kl_paged_decode_attention",
         "kl_paged_decode_read_status",
         "kl_paged_decode_noalloc",
+        "kl_paged_decode_noalloc_read_status",
         "kl_paged_kv_append",
         "kl_paged_decode_fp8",
         "kl_paged_kv_append_fp8",

@@ -80,6 +80,53 @@ def test_noalloc_consecutive_calls_of_different_shapes():
         assert (got.float() - with_scratch(q, kv).float()).abs().max().item() <= NORTH_STAR_MAX_ABS[torch.bfloat16]
 
 
+def test_noalloc_matches_the_oracle():
+    """The no-allocation path against the fp32 oracle itself, not only against the other entry
+    point: ragged lengths around page boundaries, Llama-3-8B heads, two calls in a row."""
+    from oracle import oracle
+    from kernel_lab.kv_cache import random_paged_pool
+    from tests.conftest import assert_within_abs_or_ulp, to_f32_numpy
+
+    lens = [1, 15, 16, 17, 300, 1025, 2048, 4095]
+    q, kv = random_paged_pool(lens, 32, 8, 128, 16, dtype=torch.bfloat16, device="cuda", seed=12)
+    table = kv.block_table.cpu().numpy()
+    want = oracle.paged_decode_attention(
+        to_f32_numpy(q), to_f32_numpy(kv.k_cache), to_f32_numpy(kv.v_cache), table, kv.seq_lens.cpu().numpy(),
+        None, "f32",
+    )
+    for _ in range(2):
+        got = torch.full_like(q, float("nan"))
+        assert noalloc(got, q, kv) == 0
+        torch.cuda.synchronize()
+        assert_within_abs_or_ulp(got, want, torch.bfloat16)
+
+
+def test_noalloc_status_reader_reports_a_bad_page():
+    """Status bits of a no-allocation call are read from the library's own array: a block-table
+    entry past the pool is skipped and flagged KL_STATUS_BAD_PAGE, and the next call clears it."""
+    import ctypes as C
+
+    from kernel_lab import capi
+    from kernel_lab.kv_cache import random_paged_pool
+
+    lib = capi.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    q, kv = random_paged_pool([100, 40], 32, 8, 128, 16, dtype=torch.bfloat16, device="cuda", seed=13)
+    bad = kv.block_table.clone()
+    bad[1, 1] = kv.k_cache.shape[0] + 5  # outside the pool: never followed
+    bad_kv = type(kv)(kv.k_cache, kv.v_cache, bad, kv.seq_lens, 16)
+    out = torch.empty_like(q)
+    status = C.c_uint32(0xFFFF)
+    assert noalloc(out, q, bad_kv) == 0
+    assert lib.kl_paged_decode_noalloc_read_status(C.byref(status), 0, stream) == 0
+    assert status.value == capi.KL_STATUS_BAD_PAGE
+    assert noalloc(out, q, kv) == 0  # a clean call starts from a cleared word
+    assert lib.kl_paged_decode_noalloc_read_status(C.byref(status), 1, stream) == 0
+    assert status.value == 0
+    # Sequence 0 never touches the bad entry: its output is still right.
+    assert torch.equal(out[0], with_scratch(q, kv)[0])
+
+
 def test_noalloc_rejects_problems_beyond_its_scratch():
     from kernel_lab import capi
 
