@@ -8,18 +8,25 @@ For N > 1 launch one process per GPU:
 
 Workload (default ``decode``): kernel-lab's headline, paged decode attention with Llama-3-8B
 heads (32 query / 8 KV, head_dim 128, 16-token pages), bf16, batch 64, context 4096,
-shuffled pages, NaN-poisoned spare pages. A step is one decode call. At N GPUs the batch
-grows to 64*N and every rank decodes its own 64 sequences with every head: sequences are
-independent, so there is no collective, and every GPU streams the same 1.07 GB of KV per
-step (weak scaling). ``decode_fp8``: the same with an e4m3 KV cache (per-KV-head scales; KV
-bytes counted at one per element). ``decode70b``: Llama-3-70B heads (64/8), batch 256, context 8192,
-total work fixed across N (strong scaling) in the tensor-parallel layout: KV heads sharded
-N ways and the outputs all-gathered with NCCL inside the step. ``rmsnorm``: fused add +
-RMSNorm, 4096 x 8192 bf16.
+shuffled pages, NaN-poisoned spare pages. A step is one decode call. At N GPUs the batch grows
+to 64*N and the KV heads are sharded N ways (tensor parallel): rank r holds KV heads
+[r*8/N, (r+1)*8/N) of every sequence and their query heads, so every GPU streams the same
+1.07 GB of KV per step (weak scaling), and the decode kernel itself stores its heads into every
+rank's [64*N, 32, 128] output over NVLink (one launch per step does attention and gather). The
+default line at N=1 also carries ``grid`` (config 3's six batch x context cells) and
+``secondary`` (fused add + RMSNorm, 4096 x 8192 bf16).
+
+Other workloads: ``decode_seq`` (the headline with the batch split by sequence at N > 1: no
+exchange at all); ``decode_fp8`` (the headline over an e4m3 KV cache, per-KV-head scales, KV
+bytes counted at one per element); ``decode70b`` (Llama-3-70B heads 64/8, batch 256, context
+8192, total work fixed across N: strong scaling over the same KV-head shards and fused gather);
+``cascade`` (64 sequences per GPU sharing a 4096-token prefix, 512 own tokens each); ``ragged``
+(config 4: batch 128, lengths uniform in [1, 32768] plus 16k-1, 16k, 16k+1, in the MQA 32/1,
+GQA 32/8 and MHA 32/32 layouts, one GPU); ``rmsnorm`` (fused add + RMSNorm, 4096 x 8192 bf16).
 
 One JSON line on rank 0: value = aggregate algorithmic HBM GB/s (K+V read once, q and
 out once: kernel-lab's byte model) over the max-over-ranks device time; ``roofline`` for
-the decode kernel (its own CUDA-event time); ``e2e`` through the torch op with pinned host
+the decode kernel (its own CUDA-event time); ``e2e`` through the public API with pinned host
 inputs copied in and the output copied out every step; ``cpu_baseline`` = the oracle
 (NumPy restatement of kernel-lab's PyTorch CPU reference) on this host's cores.
 ``--impl reference`` times that CPU path alone (kernel-lab's own implementation of the
@@ -30,6 +37,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import sys
@@ -45,7 +53,10 @@ RMS_METRIC = "fused add+RMSNorm % of B200 peak HBM BW (4096 tokens x 8192 hidden
 FP8_METRIC = "paged decode attn, e4m3 KV cache, algorithmic HBM GB/s (Llama-3-8B GQA bs64 ctx4096); us/call"
 CASCADE_METRIC = ("cascade (shared-prefix) decode, unique KV bytes GB/s (Llama-3-8B GQA, 64 sequences sharing a "
                   "4096-token prefix + 512 own tokens each); us/call")
+RAGGED_METRIC = ("ragged-batch paged decode attn, algorithmic HBM GB/s over MQA 32/1, GQA 32/8 and MHA 32/32 "
+                 "(batch 128, lengths U[1, 32768]); us/call")
 L2_NOTE = "inputs larger than L2 (no flush needed)"
+L2_BYTES = 126 * 1024 * 1024
 
 
 def parse() -> argparse.Namespace:
@@ -54,20 +65,43 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "ours", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["decode", "decode_fp8", "decode70b", "cascade", "rmsnorm"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "decode_seq", "decode_fp8", "decode70b", "cascade", "ragged",
+                                           "rmsnorm"], default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the grid and secondary objects of the default line")
     ap.add_argument("--batch", type=int, help="override the workload's batch (per GPU for weak scaling)")
     ap.add_argument("--ctx", type=int, help="override the workload's context length")
     return ap.parse_args()
 
 
+def ragged_lens(batch: int = 128, seed: int = 4) -> list[int]:
+    """Config 4's lengths: uniform in [1, 32768] from a seed, with 16k - 1, 16k and 16k + 1."""
+    from kernel_lab.kv_cache import config4_lengths
+
+    return config4_lengths(batch, seed)
+
+
+RAGGED_LAYOUTS = {"mqa": (32, 1), "gqa": (32, 8), "mha": (32, 32)}
+
+
 def workload_spec(name: str, world: int) -> dict:
     if name == "decode":
-        # Sequences are independent: each rank decodes its own 64 with every head, no collective.
+        if world == 1:
+            return dict(kind="decode", batch=64, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
+                        layout="single",
+                        desc="paged decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64, ctx 4096")
+        # KV heads sharded N ways, batch 64 per GPU's worth of KV, heads gathered by the kernel.
+        return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
+                    layout="kv_heads",
+                    desc=f"paged decode, Llama-3-8B heads 32/8/128 sharded {world} ways by KV head, page 16, bf16, "
+                         f"batch {64 * world} (64 per GPU of KV), ctx 4096, heads gathered over NVLink by the kernel")
+    if name == "decode_seq":
+        # Sequences are independent: each rank decodes its own 64 with every head, no exchange.
         return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
                     layout="sequences",
-                    desc="paged decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU, ctx 4096")
+                    desc="paged decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU split by sequence, "
+                         "ctx 4096")
     if name == "decode_fp8":
         # The headline with an e4m3 KV cache (per-KV-head scales): half the KV bytes per token.
         return dict(kind="decode", batch=64 * world, ctx=4096, hq=32, hkv=8, d=128, page=16, scaling="weak",
@@ -81,10 +115,14 @@ def workload_spec(name: str, world: int) -> dict:
                     desc="cascade decode, Llama-3-8B heads 32/8/128, page 16, bf16, batch 64/GPU sharing a "
                          "4096-token prefix, 512 own tokens each")
     if name == "decode70b":
-        # Tensor-parallel layout: KV heads sharded, one all-gather of the outputs per step.
+        # Tensor-parallel layout: KV heads sharded, heads gathered by the kernel; total work fixed.
         return dict(kind="decode", batch=256, ctx=8192, hq=64, hkv=8, d=128, page=16, scaling="strong",
                     layout="kv_heads",
                     desc="paged decode, Llama-3-70B heads 64/8/128, page 16, bf16, batch 256, ctx 8192")
+    if name == "ragged":
+        return dict(kind="ragged", batch=128, d=128, page=16, scaling="weak", layout="single",
+                    desc="ragged paged decode, batch 128, lengths U[1, 32768] + 16k-1/16k/16k+1 (seed 4), "
+                         "MQA 32/1, GQA 32/8, MHA 32/32 heads of 128, page 16, bf16")
     return dict(kind="rmsnorm", rows=4096, hidden=8192, scaling="weak",
                 desc="fused residual-add + RMSNorm, 4096 x 8192 bf16, eps 1e-5")
 
@@ -160,11 +198,21 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- CPU side
 
 
+def cpu_unit_spec(spec: dict) -> dict:
+    """The decode workload a CPU sample unit comes from: one sequence of the workload's shape (a
+    ragged batch: a GQA sequence of its mean length, 16384)."""
+    if spec["kind"] == "ragged":
+        return dict(spec, kind="decode", ctx=16384, hq=32, hkv=8)
+    return spec
+
+
 def cpu_measure(kind: str, spec: dict, seconds: float, dtype: str = "bf16", warmup: int = 1) -> dict:
     """The oracle on this host: whole sample units per step, until `seconds` of timed work."""
     from oracle.oracle import decode_bytes
     from oracle.timing import CpuOracleRunner
 
+    spec = cpu_unit_spec(spec)
+    kind = spec["kind"] if kind != "rmsnorm" else kind
     if kind == "decode":
         unit = dict(ctx=spec["ctx"], hq=spec["hq"] // spec.get("tp", 1), hkv=spec["hkv"] // spec.get("tp", 1),
                     d=spec["d"], page=spec["page"], dtype=dtype)
@@ -200,6 +248,8 @@ def run_reference(args, spec: dict) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    metric = RAGGED_METRIC if spec["kind"] == "ragged" else METRIC
+    spec = cpu_unit_spec(spec)
     kind = spec["kind"]
     from oracle.timing import CpuOracleRunner
 
@@ -219,7 +269,7 @@ def run_reference(args, spec: dict) -> None:
     total = sum(times)
     value = workers * len(times) * unit_bytes / total / 1e9
     line = {
-        "metric": METRIC if kind == "decode" else RMS_METRIC,
+        "metric": metric if kind == "decode" else RMS_METRIC,
         "value": value,
         "unit": "GB/s",
         "n_gpus": args.gpus,
@@ -257,12 +307,161 @@ def load_traffic(key: str) -> float | None:
         return None
 
 
+def time_back_to_back(fn, steps: int, stream) -> float:
+    """Milliseconds per call of `steps` back-to-back calls, CUDA events on the launching stream."""
+    import torch
+
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for i in range(steps):
+        fn(i)
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def decode_grid(dev, stream, steps: int, peak: float) -> dict:
+    """Config 3's grid (batch {1, 8, 64} x context {512, 4096}, 32/8/128 heads, bf16) on one GPU.
+    A cell smaller than L2 rotates over R disjoint replicas of itself (other sequences, other
+    pages) whose KV totals more than twice L2, so no launch finds its pages in L2."""
+    import torch
+
+    from kernel_lab.kv_cache import random_paged_pool
+    from kernel_lab.roofline import decode_attention_work
+
+    op = torch.ops.kernel_lab.paged_decode_attention
+    cells = {}
+    for B in (1, 8, 64):
+        for ctx in (512, 4096):
+            w = decode_attention_work([ctx] * B, 32, 8, 128, 2, 2)
+            R = max(1, math.ceil(2 * L2_BYTES / w.bytes))
+            q, kv = random_paged_pool([ctx] * (B * R), 32, 8, 128, 16, dtype=torch.bfloat16, device=dev,
+                                      seed=100 + B + ctx)
+            reps = [(q[r * B:(r + 1) * B], kv.block_table[r * B:(r + 1) * B], kv.seq_lens[r * B:(r + 1) * B],
+                     torch.empty_like(q[:B])) for r in range(R)]
+            scale = 128**-0.5
+
+            def call(i, reps=reps, kv=kv, scale=scale):
+                qq, bt, ln, out = reps[i % len(reps)]
+                op(out, qq, kv.k_cache, kv.v_cache, bt, ln, scale)
+
+            for i in range(max(3, R)):
+                call(i)
+            n = max(steps, R)
+            ms = time_back_to_back(call, n, stream)
+            gbs = w.bytes / (ms * 1e-3) / 1e9
+            cells[f"b{B}_ctx{ctx}"] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                                       "algorithmic_bytes": int(w.bytes), "replicas": R}
+            del q, kv, reps
+            torch.cuda.empty_cache()
+    return cells
+
+
+def rmsnorm_secondary(dev, stream, steps: int, peak: float) -> dict:
+    """Fused add + RMSNorm at 4096 x 8192 bf16 (x, residual ~ N(0,1), weight ~ N(1, 0.1), eps 1e-5),
+    back-to-back launches; x, residual and out total 192 MB, more than L2."""
+    import torch
+
+    from kernel_lab.roofline import rms_norm_work
+
+    R, H = 4096, 8192
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+    res = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    op = torch.ops.kernel_lab.fused_add_rms_norm
+    for _ in range(3):
+        op(out, x, res, w, 1e-5)
+    ms = time_back_to_back(lambda i: op(out, x, res, w, 1e-5), max(steps, 20), stream)
+    work = rms_norm_work(R, H, 2, True)
+    gbs = work.bytes / (ms * 1e-3) / 1e9
+    return {"metric": RMS_METRIC, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "algorithmic_bytes": int(work.bytes), "kernel": "rmsnorm_row_regs", "timing": "back-to-back launches"}
+
+
+class DecodeE2E:
+    """End to end through the public API, the way a serving loop runs: two device slots; step i's
+    q, block table and lengths go up from pinned host memory on a copy-in stream and its whole
+    output comes back on a copy-out stream, so copies overlap the neighbouring steps' kernels. The
+    KV cache stays resident. `decode(q, bt, ln, out_slot)` returns the output tensor to copy out."""
+
+    def __init__(self, decode, q, bt, ln, out_shape, dev, stream):
+        import torch
+
+        self.torch = torch
+        self.decode = decode
+        self.stream = stream
+        self.q_h = q.cpu().pin_memory()
+        self.bt_h = bt.cpu().pin_memory()
+        self.ln_h = ln.cpu().pin_memory()
+        self.out_hs = [torch.empty(out_shape, dtype=q.dtype).pin_memory() for _ in range(2)]
+        self.slots = [dict(q=torch.empty_like(q), bt=torch.empty_like(bt), ln=torch.empty_like(ln),
+                           out=torch.empty_like(q), inputs_free=None, out_read=None) for _ in range(2)]
+        self.s_in, self.s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        self.h2d = self.q_h.numel() * self.q_h.element_size() + self.bt_h.numel() * 4 + self.ln_h.numel() * 4
+        self.d2h = self.out_hs[0].numel() * self.out_hs[0].element_size()
+        self.count = 0
+
+    def step(self):
+        torch = self.torch
+        i = self.count
+        self.count += 1
+        sl = self.slots[i % 2]
+        with torch.cuda.stream(self.s_in):
+            if sl["inputs_free"] is not None:
+                self.s_in.wait_event(sl["inputs_free"])  # the kernel two steps back is done with them
+            sl["q"].copy_(self.q_h, non_blocking=True)
+            sl["bt"].copy_(self.bt_h, non_blocking=True)
+            sl["ln"].copy_(self.ln_h, non_blocking=True)
+            arrived = torch.cuda.Event()
+            arrived.record(self.s_in)
+        self.stream.wait_event(arrived)
+        if sl["out_read"] is not None:
+            self.stream.wait_event(sl["out_read"])  # the copy-out two steps back has read its output
+        src = self.decode(sl["q"], sl["bt"], sl["ln"], sl["out"])
+        done = torch.cuda.Event()
+        done.record(self.stream)
+        sl["inputs_free"] = done
+        with torch.cuda.stream(self.s_out):
+            self.s_out.wait_event(done)
+            self.out_hs[i % 2].copy_(src, non_blocking=True)
+            read = torch.cuda.Event()
+            read.record(self.s_out)
+        sl["out_read"] = read
+
+    def join(self):
+        for sl in self.slots:
+            if sl["out_read"] is not None:
+                self.stream.wait_event(sl["out_read"])
+
+    def run(self, steps: int) -> float:
+        """Milliseconds per step over `steps` pipelined steps (after 3 untimed ones)."""
+        torch = self.torch
+        for _ in range(3):
+            self.step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        self.s_in.wait_event(e0)  # no copy of the timed steps starts before the region does
+        for _ in range(steps):
+            self.step()
+        self.join()
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def last_output(self):
+        return self.out_hs[(self.count - 1) % 2]
+
+
 def main() -> None:
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     spec = workload_spec(args.workload, world)
-    if args.batch and spec["kind"] == "decode":
-        spec["batch"] = args.batch * (world if spec["scaling"] == "weak" else 1)
+    if args.batch and spec["kind"] in ("decode", "ragged"):
+        spec["batch"] = args.batch * (world if spec["scaling"] == "weak" and spec["kind"] == "decode" else 1)
         spec["desc"] += f" (batch overridden: {args.batch})"
     if args.ctx and spec["kind"] == "decode":
         spec["ctx"] = args.ctx
@@ -273,12 +472,14 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args, spec)
         return
+    if spec["kind"] == "ragged" and world > 1:
+        raise SystemExit("the ragged workload runs on one GPU")
 
     import torch
     import torch.distributed as dist
 
     from kernel_lab import cuda_ops
-    from kernel_lab.roofline import B200_SPEC_HBM_GBPS, decode_attention_work, measured_peaks, rms_norm_work
+    from kernel_lab.roofline import B200_SPEC_HBM_GBPS, Work, decode_attention_work, measured_peaks, rms_norm_work
 
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -292,13 +493,17 @@ def main() -> None:
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream()
     peaks = measured_peaks()
+    steps = args.steps
+    warmup = max(args.warmup, 3)
+    gather = None
+    extra = {}
 
     if spec["kind"] == "decode":
         from kernel_lab.kv_cache import random_paged_pool
-        from kernel_lab.sharding import batch_range, gather_heads, kv_head_range
+        from kernel_lab.sharding import PeerHeadGather, batch_range, kv_head_range
 
         B, ctx, hq, hkv, d, page = (spec[k] for k in ("batch", "ctx", "hq", "hkv", "d", "page"))
-        gather = spec["layout"] == "kv_heads" and world > 1
+        scale = d**-0.5
         if spec["layout"] == "kv_heads":
             lo, hi = kv_head_range(hkv, world, rank)
             b_local = B
@@ -319,26 +524,29 @@ def main() -> None:
             q, kv = random_paged_pool([ctx] * b_local, hq, hkv, d, page, dtype=torch.bfloat16, device=dev,
                                       seed=1234 + rank)
         hq_l, hkv_l = q.shape[1], kv.k_cache.shape[2]
-        scale = d**-0.5
-        out_local = torch.empty_like(q)
-        out_full = torch.empty((B, hq, d), dtype=q.dtype, device=dev) if gather else None
         kv_bytes = 1 if spec.get("kv8") else 2
         kernel_work = decode_attention_work([ctx] * b_local, hq_l, hkv_l, d, 2, kv_bytes)  # per rank, per launch
         job_bytes = decode_attention_work([ctx] * B, hq, hkv, d, 2, kv_bytes).bytes
         if spec.get("cascade"):
-            from kernel_lab.roofline import Work
-
             # Unique KV bytes: each GPU's shared prefix once plus every sequence's own tokens.
             prefix_kv = spec["prefix"] * hkv * d * 2 * 2
             kernel_work = Work(kernel_work.bytes + prefix_kv,
                                kernel_work.flops + 4 * spec["prefix"] * b_local * hq * d)
             job_bytes += prefix_kv * world
-        if spec.get("cascade"):
+        if spec["layout"] == "kv_heads" and world > 1:
+            # The product path at N > 1: one launch per step decodes this rank's KV heads and stores
+            # its heads into every rank's output over NVLink.
+            gather = PeerHeadGather(B, hq_l, d, torch.bfloat16)
+
+            def decode_op(out_t, q_t, bt_t, ln_t):
+                return gather(q_t, kv.k_cache, kv.v_cache, bt_t, ln_t, scale)
+        elif spec.get("cascade"):
 
             def decode_op(out_t, q_t, bt_t, ln_t):
                 torch.ops.kernel_lab.paged_decode_attention_cascade(
                     out_t, q_t, kv.k_cache, kv.v_cache, ckv.prefix_block_table, ckv.prefix_lens, ckv.prefix_indptr,
                     bt_t, ln_t, scale, None, None)
+                return out_t
         elif spec.get("kv8"):
             from kernel_lab.kv_cache import e4m3_scales, quantize_e4m3
 
@@ -350,20 +558,34 @@ def main() -> None:
             def decode_op(out_t, q_t, bt_t, ln_t):
                 torch.ops.kernel_lab.paged_decode_attention_fp8(out_t, q_t, kv.k_cache, kv.v_cache, k_scale, v_scale,
                                                                 bt_t, ln_t, scale)
+                return out_t
         else:
 
             def decode_op(out_t, q_t, bt_t, ln_t):
                 torch.ops.kernel_lab.paged_decode_attention(out_t, q_t, kv.k_cache, kv.v_cache, bt_t, ln_t, scale)
+                return out_t
 
-        def kernel():
-            decode_op(out_local, q, kv.block_table, kv.seq_lens)
+        out_local = torch.empty_like(q)
+        result = [None]
 
-        def step():
-            kernel()
-            if gather:
-                gather_heads(out_local, world, out=out_full)
+        def step(i=0):
+            result[0] = decode_op(out_local, q, kv.block_table, kv.seq_lens)
 
         metric = FP8_METRIC if spec.get("kv8") else CASCADE_METRIC if spec.get("cascade") else METRIC
+        launches_per_step = 3 if spec.get("cascade") else 1
+        problems = [(q, kv.block_table, kv.seq_lens, decode_op,
+                     (B, hq, d) if gather is not None else tuple(q.shape), job_bytes)]
+    elif spec["kind"] == "ragged":
+        from kernel_lab.kv_cache import random_paged_pool
+
+        lens = ragged_lens(spec["batch"])
+        layouts = {}
+        for name, (hq, hkv) in RAGGED_LAYOUTS.items():
+            layouts[name] = dict(hq=hq, hkv=hkv, work=decode_attention_work(lens, hq, hkv, 128, 2, 2))
+        kernel_work = Work(sum(v["work"].bytes for v in layouts.values()), sum(v["work"].flops for v in layouts.values()))
+        job_bytes = kernel_work.bytes
+        metric = RAGGED_METRIC
+        launches_per_step = 3
     else:
         R, H = spec["rows"], spec["hidden"]
         g = torch.Generator(device=dev).manual_seed(7)
@@ -374,151 +596,143 @@ def main() -> None:
         kernel_work = rms_norm_work(R, H, 2, True)
         job_bytes = kernel_work.bytes * world
 
-        def kernel():
+        def step(i=0):
             torch.ops.kernel_lab.fused_add_rms_norm(out, x, res, w, 1e-5)
 
-        step = kernel
         metric = RMS_METRIC
+        launches_per_step = 1
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    if spec["kind"] == "ragged":
+        # Each layout's pool is built, timed over the same K steps and freed in turn (MHA alone holds
+        # 37 GB of KV); a step of the workload is one call per layout, so its time is their sum.
+        step_ms = 0.0
+        clock_samples = []
+        e2e_ms = 0.0
+        h2d = d2h = 0
+        for name, lay in layouts.items():
+            q, kv = random_paged_pool(lens, lay["hq"], lay["hkv"], 128, 16, dtype=torch.bfloat16, device=dev, seed=4)
+            out_l = torch.empty_like(q)
 
-    # ---- timed region: exactly K steps, CUDA events on the launching stream. On one GPU a
-    # step is exactly one launch of the kernel, so the region's two events give the kernel's
-    # average launch duration (an event between back-to-back launches would add ~5 us of
-    # launch gap to every step); with a gather in the step, events bracket each kernel too.
-    per_kernel = spec["kind"] == "decode" and gather
-    n_ev = args.steps if per_kernel else 0
-    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        torch.cuda.synchronize()
-        t0.record(stream)
-        for i in range(args.steps):
-            if per_kernel:
-                k_start[i].record(stream)
-                kernel()
-                k_end[i].record(stream)
-                gather_heads(out_local, world, out=out_full)
-            else:
-                step()
-        t1.record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    step_ms = t0.elapsed_time(t1) / args.steps
-    if per_kernel:
-        kern_ms = sum(a.elapsed_time(b) for a, b in zip(k_start, k_end, strict=True)) / args.steps
-    else:
+            def one(i=0, q=q, kv=kv, out_l=out_l):
+                torch.ops.kernel_lab.paged_decode_attention(out_l, q, kv.k_cache, kv.v_cache, kv.block_table,
+                                                            kv.seq_lens, 128**-0.5)
+
+            for _ in range(warmup):
+                one()
+            with ClockSampler(torch.cuda.current_device()) as clocks:
+                ms = time_back_to_back(one, steps, stream)
+            clock_samples.append(clocks)
+            step_ms += ms
+            gbs = lay["work"].bytes / (ms * 1e-3) / 1e9
+            lay.update(us=round(ms * 1e3, 2), gbs=round(gbs, 1), frac=round(gbs / peaks.hbm_gbps, 4),
+                       kv_bytes=int(lay["work"].bytes), status=cuda_ops.decode_status(clear=True))
+
+            def dec(q_t, bt_t, ln_t, out_t, kv=kv):
+                torch.ops.kernel_lab.paged_decode_attention(out_t, q_t, kv.k_cache, kv.v_cache, bt_t, ln_t, 128**-0.5)
+                return out_t
+
+            e2e = DecodeE2E(dec, q, kv.block_table, kv.seq_lens, tuple(q.shape), dev, stream)
+            lay_e2e = e2e.run(max(10, min(steps, 50)))
+            resident = out_l.cpu()
+            if not torch.equal(e2e.last_output(), resident):
+                raise SystemExit(f"ragged {name}: e2e output differs from the device-resident step's output")
+            e2e_ms += lay_e2e
+            h2d += e2e.h2d
+            d2h += e2e.d2h
+            lay["e2e_us"] = round(lay_e2e * 1e3, 2)
+            del lay["work"], q, kv, out_l, e2e
+            torch.cuda.empty_cache()
         kern_ms = step_ms
-    tt = torch.tensor([step_ms, kern_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    step_ms, kern_ms = tt.tolist()
-
-    # ---- end to end through the torch op: pinned host inputs in, result out, every step
-    e2e = None
-    if spec["kind"] == "decode":
-        # A serving loop's shape: two device slots; step i's inputs go up on a copy-in stream
-        # and its output comes back on a copy-out stream, so copies overlap the neighbouring
-        # steps' kernels. Every step still copies its own q, block table and lengths in and
-        # its whole output out; the KV cache stays resident.
-        q_h = q.cpu().pin_memory()
-        bt_h = kv.block_table.cpu().pin_memory()
-        ln_h = kv.seq_lens.cpu().pin_memory()
-        out_shape = out_full.shape if gather else out_local.shape
-        out_hs = [torch.empty(out_shape, dtype=q.dtype).pin_memory() for _ in range(2)]
-        slots = [dict(q=torch.empty_like(q), bt=torch.empty_like(kv.block_table), ln=torch.empty_like(kv.seq_lens),
-                      out=torch.empty_like(out_local),
-                      full=torch.empty(out_shape, dtype=q.dtype, device=dev) if gather else None,
-                      inputs_free=None, out_read=None) for _ in range(2)]
-        s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-        h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + ln_h.numel() * 4
-        d2h = out_hs[0].numel() * out_hs[0].element_size()
-        e2e_count = [0]
-
-        def e2e_step():
-            i = e2e_count[0]
-            e2e_count[0] += 1
-            sl = slots[i % 2]
-            with torch.cuda.stream(s_in):
-                if sl["inputs_free"] is not None:
-                    s_in.wait_event(sl["inputs_free"])  # the kernel two steps back is done with them
-                sl["q"].copy_(q_h, non_blocking=True)
-                sl["bt"].copy_(bt_h, non_blocking=True)
-                sl["ln"].copy_(ln_h, non_blocking=True)
-                arrived = torch.cuda.Event()
-                arrived.record(s_in)
-            stream.wait_event(arrived)
-            if sl["out_read"] is not None:
-                stream.wait_event(sl["out_read"])  # the copy-out two steps back has read the slot
-            decode_op(sl["out"], sl["q"], sl["bt"], sl["ln"])
-            src = gather_heads(sl["out"], world, out=sl["full"]) if gather else sl["out"]
-            done = torch.cuda.Event()
-            done.record(stream)
-            sl["inputs_free"] = done
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(done)
-                out_hs[i % 2].copy_(src, non_blocking=True)
-                read = torch.cuda.Event()
-                read.record(s_out)
-            sl["out_read"] = read
-
-        def e2e_join():
-            for sl in slots:
-                if sl["out_read"] is not None:
-                    stream.wait_event(sl["out_read"])
+        summaries = [c.summary() for c in clock_samples if c.summary()]
+        clocks_summary = None
+        if summaries:
+            clocks_summary = {"sm_mhz": statistics.median(c["sm_mhz"] for c in summaries),
+                              "sm_max_mhz": summaries[0]["sm_max_mhz"],
+                              "reasons": sorted({r for c in summaries for r in c["reasons"]}),
+                              "samples": sum(c["samples"] for c in summaries)}
+        extra["layouts"] = layouts
+        e2e_line = {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms}
+        status = sum(v["status"] for v in layouts.values())
     else:
-        x_h = x.cpu().pin_memory()
-        res_h = res.cpu().pin_memory()
-        out_h = torch.empty_like(x_h).pin_memory()
-        res_back = torch.empty_like(x_h).pin_memory()
-        h2d = 2 * x_h.numel() * 2
-        d2h = 2 * out_h.numel() * 2
+        for i in range(warmup):
+            step(i)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
 
-        def e2e_step():
-            x.copy_(x_h, non_blocking=True)
-            res.copy_(res_h, non_blocking=True)
-            torch.ops.kernel_lab.fused_add_rms_norm(out, x, res, w, 1e-5)
-            out_h.copy_(out, non_blocking=True)
-            res_back.copy_(res, non_blocking=True)
+        # ---- timed region: exactly K steps, CUDA events on the launching stream. Every step is
+        # one launch of the hot path (the fused gather included at N > 1; the cascade's three
+        # kernels excepted), so the region's two events give the kernel's average launch duration
+        # (an event between back-to-back launches would add ~5 us of launch gap to every step).
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(torch.cuda.current_device()) as clocks:
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for i in range(steps):
+                step(i)
+            t1.record(stream)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        step_ms = t0.elapsed_time(t1) / steps
+        tt = torch.tensor([step_ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        step_ms = tt.item()
+        kern_ms = step_ms
+        clocks_summary = clocks.summary()
 
-        def e2e_join():
-            pass
+        # ---- end to end through the public API: pinned host inputs in, result out, every step
+        if spec["kind"] == "decode":
+            resident = result[0].cpu()  # the timed steps' output, before the e2e steps reuse regions
+            q0, bt0, ln0, dec_op, out_shape, _ = problems[0]
+            e2e = DecodeE2E(lambda q_t, bt_t, ln_t, out_t: dec_op(out_t, q_t, bt_t, ln_t), q0, bt0, ln0, out_shape,
+                            dev, stream)
+            if world > 1:
+                dist.barrier()
+            e2e_ms_local = e2e.run(max(10, min(steps, 100)))
+            # The pipelined steps computed what the resident steps did (same inputs, deterministic
+            # kernel): a copy that raced its slot would show here.
+            if not torch.equal(e2e.last_output(), resident):
+                raise SystemExit("e2e output differs from the device-resident step's output")
+            h2d, d2h = e2e.h2d, e2e.d2h
+        else:
+            x_h = x.cpu().pin_memory()
+            res_h = res.cpu().pin_memory()
+            out_h = torch.empty_like(x_h).pin_memory()
+            res_back = torch.empty_like(x_h).pin_memory()
+            h2d = 2 * x_h.numel() * 2
+            d2h = 2 * out_h.numel() * 2
 
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(10, min(args.steps, 100))
-    e0.record(stream)
-    if spec["kind"] == "decode":
-        s_in.wait_event(e0)  # no copy of the timed steps starts before the region does
-    for _ in range(e2e_steps):
-        e2e_step()
-    e2e_join()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = te.item()
-    if spec["kind"] == "decode":
-        # The pipelined steps computed what the resident steps did (same inputs, deterministic
-        # kernel): a copy that raced its slot would show here.
-        ref = (out_full if gather else out_local).cpu()
-        if not torch.equal(out_hs[(e2e_count[0] - 1) % 2], ref):
-            raise SystemExit("e2e output differs from the device-resident step's output")
-    e2e = {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d * world),
-           "d2h_bytes_per_step": int(d2h * world), "ms_per_step": e2e_ms}
+            def e2e_step(i=0):
+                x.copy_(x_h, non_blocking=True)
+                res.copy_(res_h, non_blocking=True)
+                torch.ops.kernel_lab.fused_add_rms_norm(out, x, res, w, 1e-5)
+                out_h.copy_(out, non_blocking=True)
+                res_back.copy_(res, non_blocking=True)
 
-    status = cuda_ops.decode_status(clear=True) if spec["kind"] == "decode" else 0
+            for _ in range(3):
+                e2e_step()
+            if world > 1:
+                dist.barrier()
+            e2e_ms_local = time_back_to_back(e2e_step, max(10, min(steps, 100)), stream)
+        te = torch.tensor([e2e_ms_local], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = te.item()
+        e2e_line = {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(h2d * world),
+                    "d2h_bytes_per_step": int(d2h * world), "ms_per_step": e2e_ms}
+        if spec["kind"] == "decode":
+            status = gather.status(clear=True) if gather is not None else cuda_ops.decode_status(clear=True)
+        else:
+            status = 0
+        if spec["kind"] == "decode" and args.workload == "decode" and world == 1 and not args.no_extras:
+            extra["grid"] = decode_grid(dev, stream, min(steps, 100), peaks.hbm_gbps)
+            extra["secondary"] = rmsnorm_secondary(dev, stream, steps, peaks.hbm_gbps)
+
+    if gather is not None:
+        gather.close()
 
     if rank == 0:
         achieved = kernel_work.bytes / (kern_ms * 1e-3) / 1e9
@@ -528,23 +742,36 @@ def main() -> None:
         cpu = None
         # kernel-lab has no e4m3 or cascade path to time on the host
         if world == 1 and not args.no_cpu_baseline and not spec.get("kv8") and not spec.get("cascade"):
-            cpu = cpu_measure(spec["kind"], spec, args.cpu_seconds)
+            cpu = cpu_measure("decode" if spec["kind"] == "ragged" else spec["kind"], spec, args.cpu_seconds)
         layout = spec.get("layout")
-        parallelism = "1 gpu" if world == 1 else f"kv-head tp{world}" if layout == "kv_heads" else f"sequences dp{world}"
+        parallelism = ("1 gpu" if world == 1 else f"kv-head tp{world}" if layout == "kv_heads"
+                       else f"sequences dp{world}")
         cfg = {"workload": spec["desc"], "l2": L2_NOTE, "parallelism": parallelism}
         if spec["kind"] == "decode":
             cfg.update(batch=spec["batch"], ctx=spec["ctx"], num_q_heads=spec["hq"], num_kv_heads=spec["hkv"],
                        head_dim=spec["d"], page_size=spec["page"], pool_pages=int(kv.k_cache.shape[0]),
                        kv_bytes_per_gpu=int(kernel_work.bytes), planner="load-balanced (num_splits=0)")
+            if gather is not None:
+                cfg["gather"] = ("fused: the decode kernel stores every rank's heads into every rank's output over "
+                                 "NVLink (CUDA IPC peer stores, no multicast), one launch per step")
+        elif spec["kind"] == "ragged":
+            cfg.update(batch=spec["batch"], head_dim=128, page_size=16, lengths="U[1, 32768] seed 4 + 16383/16384/16385",
+                       layouts={k: f"{v['hq']}/{v['hkv']}" for k, v in RAGGED_LAYOUTS.items()})
         else:
             cfg.update(rows=spec["rows"], hidden=spec["hidden"], eps=1e-5)
+        if "grid" in extra:
+            cfg["grid_l2"] = "cells smaller than 2x L2 rotate over disjoint replicas totalling more than 2x L2"
+        kernel_name = ("cascade_prefix_kernel + cascade_prefix_reduce_kernel + decode_tc_kernel (the whole op)"
+                       if spec.get("cascade") else "decode_tc_kernel (attention and head gather in one launch)"
+                       if gather is not None else "decode_tc_kernel" if spec["kind"] in ("decode", "ragged")
+                       else "rmsnorm_row_regs")
         line = {
             "metric": metric,
             "value": value,
             "unit": "GB/s",
             "n_gpus": world,
-            "steps": args.steps,
-            "warmup": max(args.warmup, 3),
+            "steps": steps,
+            "warmup": warmup,
             "ms_per_step": step_ms,
             "us_per_call": kern_ms * 1e3,
             "pct_of_spec_peak_hbm": 100 * achieved / B200_SPEC_HBM_GBPS,
@@ -552,7 +779,7 @@ def main() -> None:
             "scaling": spec["scaling"],
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) q/K/V, shuffled pages, NaN spare pages)" if spec["kind"] == "decode"
+            "data": "synthetic (seeded N(0,1) q/K/V, shuffled pages, NaN spare pages)" if spec["kind"] != "rmsnorm"
             else "synthetic (seeded x, residual ~ N(0,1), weight ~ N(1, 0.1))",
             "impl": "b200",
             "config": cfg,
@@ -565,17 +792,17 @@ def main() -> None:
                 "peak_source": f"{peaks.source} (MEASURED_PEAKS.json hbm_gbs, copy burst)"
                 if peaks.source == "measured" else "fallback 6650 GB/s",
                 "traffic": traffic,
-                "algorithmic_bytes_per_launch": int(kernel_work.bytes),
-                "kernel": ("cascade_prefix_kernel + cascade_prefix_reduce_kernel + decode_tc_kernel (the whole op)"
-                           if spec.get("cascade") else "decode_tc_kernel" if spec["kind"] == "decode"
-                           else "rmsnorm_row_regs"),
+                "algorithmic_bytes_per_launch": int(kernel_work.bytes) if spec["kind"] != "ragged"
+                else "per layout, see layouts",
+                "kernel": kernel_name,
             },
             "cpu_baseline": cpu,
-            "e2e": e2e,
-            "clocks": clocks.summary(),
-            "gpu_launches": args.steps * (3 if spec.get("cascade") else 1),
+            "e2e": e2e_line,
+            "clocks": clocks_summary,
+            "gpu_launches": steps * launches_per_step,
             "status_bits": status,
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -40,7 +40,8 @@ enum {
   KL_STATUS_BAD_PAGE = 1,     /* a block-table entry outside [0, num_pages): that page was skipped */
   KL_STATUS_LEN_CLAMPED = 2,  /* a sequence longer than max_pages_per_seq * page_size was clamped */
   KL_STATUS_WAIT_TIMEOUT = 4,  /* an internal pipeline wait exceeded its time limit; output is invalid */
-  KL_STATUS_BAD_PREFIX_GROUPS = 8  /* cascade: prefix_indptr is not a partition of the batch; prefixes ignored */
+  KL_STATUS_BAD_PREFIX_GROUPS = 8, /* cascade: prefix_indptr is not a partition of the batch; prefixes ignored */
+  KL_STATUS_PEER_TIMEOUT = 16      /* head gather: another rank's arrival did not come within 10 s */
 };
 
 /* Library version string, e.g. "kernel_lab_b200 0.1.0 sm_100a". */
@@ -113,6 +114,64 @@ int kl_paged_decode_attention(int dtype, void* out, const void* q, const void* k
  * if clear != 0, reset it to zero.
  */
 int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* stream);
+
+/*
+ * Multi-GPU decode sharded by KV head (tensor parallel; one process per GPU of one node), with
+ * the head gather fused into the decode kernel. Rank r of N holds KV heads [r*Hkv, (r+1)*Hkv)
+ * of the pool (its own contiguous NHD pool of Hkv heads) and their query heads
+ * [r*Hq, (r+1)*Hq) of q; num_q_heads / num_kv_heads below are these per-rank counts. Every
+ * rank's output is the whole [batch, N*num_q_heads, head_dim]: the kernel stores each final row
+ * into this rank's output and, with plain stores over NVLink, into every other rank's, at this
+ * rank's head offset. The last CTA to finish on a GPU then publishes the call's epoch into every
+ * rank's flags and waits until all N ranks have published it, so when the call completes on a
+ * rank's stream that rank's output holds every head. No NCCL call, no copy, no multicast.
+ *
+ * Buffers: out[r] and flags[r] are rank r's output and flags as mapped in this process (through
+ * kl_ipc_open for r != rank); flags[r] is uint32[N], done is one uint32 of this rank; both start
+ * at zero (kl_ipc_alloc zeroes its memory). epoch must be the same on every rank for the same
+ * call, start at 1 and grow by one per call. Ranks must be on distinct GPUs (they wait on one
+ * another) and make the same calls in the same order. Peers write a rank's output while that
+ * rank may still be reading an earlier call's: call e + 1 of a peer can run once every rank has
+ * arrived at call e. Alternate the output regions by epoch: two regions when every reader of a
+ * call's output is stream-ordered before the rank's next call, three when a reader (a copy on
+ * another stream, say) only has to finish before the call after next. A rank whose peers do not
+ * arrive within 10 s sets KL_STATUS_PEER_TIMEOUT in `sync` and returns (its output is then
+ * incomplete).
+ * num_ranks == 1: plain kl_paged_decode into out[0].
+ *
+ * Tensor-core shapes only (fp16/bf16, head_dim 64/128/256, page size 8 or a multiple of 16, the
+ * pointers 16-byte aligned); other calls return cudaErrorNotSupported. Scratch as for
+ * kl_paged_decode with the per-rank shape. No counterpart in kernel-lab (single-GPU).
+ */
+#define KL_GATHER_MAX_RANKS 8
+#define KL_IPC_HANDLE_BYTES 64
+
+typedef struct kl_head_gather {
+  int num_ranks;
+  int rank;
+  uint32_t epoch;
+  void* out[KL_GATHER_MAX_RANKS];
+  uint32_t* flags[KL_GATHER_MAX_RANKS];
+  uint32_t* done;
+} kl_head_gather_t;
+
+int kl_paged_decode_gather(int dtype, const kl_head_gather_t* gather, const void* q, const void* k_cache,
+                           const void* v_cache, const int32_t* block_table, const int32_t* seq_lens, int batch,
+                           int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                           int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages, float scale,
+                           void* partials, size_t partial_bytes, void* sync, size_t sync_bytes, void* stream);
+
+/*
+ * Device memory another process of this node can map (CUDA IPC; plain peer mappings, no
+ * multicast): kl_ipc_alloc allocates `bytes` on the current device, zeroes them and writes the
+ * KL_IPC_HANDLE_BYTES-byte handle a peer passes to kl_ipc_open to map them (on its own current
+ * device, peer access enabled). kl_ipc_close unmaps a peer's buffer; kl_ipc_free frees one's own.
+ * These are set-up calls (they synchronise); no counterpart in kernel-lab.
+ */
+int kl_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int kl_ipc_open(const void* handle, void** ptr);
+int kl_ipc_close(void* ptr);
+int kl_ipc_free(void* ptr);
 
 /* Bytes of device memory the library reserves per GPU for kl_paged_decode_noalloc. */
 #define KL_NOALLOC_SCRATCH_BYTES ((16u << 20) + (256u << 10))

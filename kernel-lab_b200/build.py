@@ -79,7 +79,10 @@ def run(cmd: list[str], verbose: bool) -> None:
 def build_library(force: bool = False, verbose: bool = False) -> Path:
     nvcc = str(cuda_home() / "bin" / "nvcc")
     OBJ_DIR.mkdir(exist_ok=True)
-    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}"]
+    # --split-compile: the device compilation of one file runs on every core (the decode file's
+    # kernel instantiations take minutes on one).
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}",
+             "--split-compile=0"]
     objs = []
     jobs = []
     for src in CU_SOURCES:

@@ -129,6 +129,7 @@ enum StatusBits : uint32_t {
   kStatusLenClamped = 2u,    // a sequence longer than max_pages * page_size was clamped
   kStatusWaitTimeout = 4u,   // an mbarrier wait ran out of time; the kernel stopped early
   kStatusBadPrefixGroups = 8u,  // cascade groups do not partition the batch: prefixes were ignored
+  kStatusPeerTimeout = 16u,     // head gather: a rank's arrival did not come within the time limit
 };
 
 // ----------------------------------------------------------------- programmatic dependent launch
@@ -272,6 +273,28 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
 }
 
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// System-scope forms, for flags that other GPUs read or write over NVLink (peer memory mapped
+// into this process): a fence that orders this thread's earlier stores (local and remote) before
+// its later ones, a releasing store and an acquiring load.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Nanoseconds of the GPU's global timer (wall-clock time limits for waits on other GPUs).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 // ----------------------------------------------------------------- TMA
 

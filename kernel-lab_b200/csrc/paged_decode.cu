@@ -51,6 +51,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -71,6 +72,22 @@ constexpr int kGenChunk = 32;     // tokens per step of the generic kernel
 constexpr int kMaxBatch = 16384;  // the plan lives in shared memory
 constexpr int kMaxHeadGroups = 4; // query-head groups per KV head (counter stride)
 constexpr uint64_t kWaitLimit = 2000000000ull;  // SM cycles: about one second at 1.9 GHz
+constexpr int kMaxRanks = KL_GATHER_MAX_RANKS;   // GPUs of one head gather
+constexpr uint64_t kPeerWaitNs = 10000000000ull; // a rank waits this long (10 s) for its peers' arrivals
+
+// Head gather over NVLink (ranks > 1): every final output row is stored to this rank's output
+// and, with plain peer stores, to the same place in every other rank's (out[r]: rank r's output
+// as mapped in this process, at this rank's head offset). The launch then ends with one
+// cross-GPU arrival: the last CTA to finish on this GPU publishes `epoch` in every rank's flags
+// and waits (bounded) until every rank has published it in this rank's flags.
+struct Gather {
+  int ranks;  // 0 or 1: no gather
+  int rank;
+  uint32_t epoch;
+  void* out[kMaxRanks];
+  uint32_t* flags[kMaxRanks];  // rank r's arrival flags [ranks]
+  uint32_t* done;              // this rank's count of finished CTAs (zero at rest)
+};
 
 struct DecodeArgs {
   void* out;
@@ -113,6 +130,11 @@ struct DecodeArgs {
   int cas_hpw;    // query rows per counter group (the decode kernel's heads per warp)
   float* cas_o;   // [cas_planes + 1][batch * num_q_heads][head_dim]: normalised partial outputs
   float* cas_lse; // [cas_planes + 1][batch * num_q_heads]: their base-2 LSEs
+  // Output placement: sequence b's query head h at out + b * out_seq_stride + h * head_dim
+  // (out_seq_stride = num_q_heads * head_dim unless out is this rank's head slice of a wider
+  // output), and the head gather (tensor-core kernel, plain decode only).
+  int64_t out_seq_stride;
+  Gather gat;
 };
 
 struct TcShape {
@@ -121,6 +143,7 @@ struct TcShape {
   int ht;      // KV heads per tile
   int hg;      // query-head groups (of 8*NT heads) per KV head
   int tw;      // warps splitting the tiles of one (head, group)
+  int ns;      // streams: TW when each warp walks its own range (one (head, group) a tile), else 1
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -153,6 +176,7 @@ struct Walk {
   bool first;       // balanced: no segment produced yet
   int item, items;  // forced
   int n, V;         // plan entries, prefix items among them
+  int vidx, vgrid;  // the walker's range: range vidx of vgrid (a CTA, or one stream of a CTA)
 };
 
 // Shared-memory plan arrays. lens/prefix have one slot per entry (+1 for prefix); hp and vstart
@@ -248,7 +272,8 @@ __device__ __forceinline__ int group_of_entry(const int* vstart, int P, int e) {
 // misc[kMiscV] = V, misc[kMiscEntries] = entries. For a cascade, also hp and vstart; a group
 // table that is not a partition of the batch (indptr[0] = 0, non-decreasing, indptr[P] = batch)
 // turns the prefixes off and sets KL_STATUS_BAD_PREFIX_GROUPS. Ends with a block barrier.
-__device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps) {
+// `streams`: ranges per CTA (the plan is cut into gridDim.x * streams ranges).
+__device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps, int streams = 1) {
   const int B = a.batch;
   const int nt = blockDim.x, tid = threadIdx.x;
   const bool report = blockIdx.x == 0;
@@ -301,7 +326,8 @@ __device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps) {
   if (tid == 0) {
     const int total = per_unit * a.units;
     misc[0] = total;
-    misc[1] = max(a.min_tiles, (total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x));
+    const int vgrid = static_cast<int>(gridDim.x) * streams;
+    misc[1] = max(a.min_tiles, (total + vgrid - 1) / vgrid);
     misc[2] = 0;
     misc[3] = 0;
     misc[kMiscV] = V;
@@ -310,18 +336,23 @@ __device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps) {
   __syncthreads();
 }
 
-__device__ __forceinline__ void walk_init(const DecodeArgs& a, const int* misc, Walk& w) {
+// Range vidx of vgrid (default: this CTA's of the grid's); plan_build must have cut the plan into
+// vgrid ranges.
+__device__ __forceinline__ void walk_init(const DecodeArgs& a, const int* misc, Walk& w, int vidx = -1,
+                                          int vgrid = -1) {
+  w.vidx = vidx >= 0 ? vidx : static_cast<int>(blockIdx.x);
+  w.vgrid = vgrid > 0 ? vgrid : static_cast<int>(gridDim.x);
   w.V = misc[kMiscV];
   w.n = misc[kMiscEntries];
   if (a.splits == 0) {
     const int total = misc[0];
     w.R = misc[1];
-    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * w.R;
+    const int64_t t0 = static_cast<int64_t>(w.vidx) * w.R;
     w.t = static_cast<int>(min(t0, static_cast<int64_t>(total)));
     w.t1 = static_cast<int>(min(t0 + w.R, static_cast<int64_t>(total)));
     w.first = true;
   } else {
-    w.item = blockIdx.x;
+    w.item = w.vidx;
     w.items = a.batch * a.units * a.splits;
   }
 }
@@ -384,7 +415,7 @@ __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const PlanSmem& p
     // The first chunk is its CTA's first segment iff that CTA's range holds no earlier tiles.
     s.first_aligned = s.c_first * w.R >= s_begin;
     s.whole = s.nchunks == 1;
-    s.chunk = w.first ? 2 * blockIdx.x : 2 * blockIdx.x + 1;
+    s.chunk = w.first ? 2 * w.vidx : 2 * w.vidx + 1;
     w.first = false;
     w.t = from + len;
     entry_members<CAS>(a, ps, w, s);
@@ -404,7 +435,7 @@ __device__ __forceinline__ bool walk_next(const DecodeArgs& a, const PlanSmem& p
   s.c_first = 0;
   s.first_aligned = true;
   s.whole = S == 1;
-  w.item += gridDim.x;
+  w.item += w.vgrid;
   entry_members<CAS>(a, ps, w, s);
   return true;
 }
@@ -424,17 +455,30 @@ __device__ __forceinline__ uint32_t* counter_of(const DecodeArgs& a, int cb, int
   return a.sync + 1 + (static_cast<int64_t>(cb) * a.num_kv_heads + kvh) * kMaxHeadGroups + hg;
 }
 
+// Stores one vector of final output at element offset `off`: to this call's output and, in a
+// head gather, to the same place in every other rank's output (plain stores over NVLink).
+template <typename T, bool GATHER, typename V>
+__device__ __forceinline__ void store_out(const DecodeArgs& a, int64_t off, const V& v) {
+  *reinterpret_cast<V*>(static_cast<T*>(a.out) + off) = v;
+  if (GATHER) {
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < a.gat.ranks && r != a.gat.rank) *reinterpret_cast<V*>(static_cast<T*>(a.gat.out[r]) + off) = v;
+    }
+  }
+}
+
 // Zero the outputs of sequences with no token at all (balanced mode has no work for them).
 // seq_len_s[b] = sequence b's own clamped length; hp (cascade only) its group's prefix length.
-template <typename T>
+template <typename T, bool GATHER>
 __device__ __forceinline__ void zero_empty_sequences(const DecodeArgs& a, const int* seq_len_s, const int* hp,
                                                      int ctid, int nthr) {
   if (a.splits != 0) return;
-  T* out = static_cast<T*>(a.out);
   const int n = a.num_q_heads * a.head_dim;
+  const T zero = Storage<T>::store(0.0f);
   for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {
     if (seq_len_s[b] != 0 || (hp != nullptr && hp[b] != 0)) continue;
-    for (int i = ctid; i < n; i += nthr) out[static_cast<int64_t>(b) * n + i] = Storage<T>::store(0.0f);
+    for (int i = ctid; i < n; i += nthr) store_out<T, GATHER>(a, static_cast<int64_t>(b) * (GATHER ? a.out_seq_stride : n) + i, zero);
   }
 }
 
@@ -453,6 +497,17 @@ __device__ __forceinline__ int64_t sink_row(const DecodeArgs& a, const RowSink& 
   m = CAS ? r / a.group : 0;  // without a cascade every row < nh belongs to member 0
   return static_cast<int64_t>(k.seq + m) * a.num_q_heads + k.kvh * a.group + (r - m * a.group);
 }
+
+// Element offset of row hl's final output (member m of the sink, as sink_row gives it). Without a
+// gather the output rows are contiguous ([batch, num_q_heads, head_dim]).
+template <bool CAS, bool GATHER>
+__device__ __forceinline__ int64_t sink_out(const DecodeArgs& a, const RowSink& k, int hl, int m) {
+  const int r = k.row0 + hl;
+  const int head = k.kvh * a.group + (r - m * a.group);
+  if (!GATHER) return (static_cast<int64_t>(k.seq + m) * a.num_q_heads + head) * a.head_dim;
+  return static_cast<int64_t>(k.seq + m) * a.out_seq_stride + static_cast<int64_t>(head) * a.head_dim;
+}
+
 
 // Row offset of a cascade side's plane: the (single) prefix plane of an in-plan prefix item, or
 // the sequence's own plane after the prefix chunk planes.
@@ -473,7 +528,7 @@ __device__ __forceinline__ int prefix_planes(const DecodeArgs& a, int prefix_len
 // chunk's lane. The result depends only on the partials, never on which chunk merges; it is
 // written as out = sum / W (zero where every chunk was empty). kernel-lab's merge formula
 // (triton_kernels/paged_attention.py:150-166).
-template <typename T, int D, int HPW, int NE, int KB, bool CAS>
+template <typename T, int D, int HPW, int NE, int KB, bool CAS, bool GATHER>
 __device__ __forceinline__ void merge_chunks_impl(const DecodeArgs& a, const Seg& s, int slots_per_chunk, int mu,
                                                   int nh, const RowSink& sink, int lane) {
   constexpr int Q = D / 4;  // float4 per head row
@@ -591,24 +646,24 @@ __device__ __forceinline__ void merge_chunks_impl(const DecodeArgs& a, const Seg
       uint2 pk;
       pk.x = Storage<T>::pack2(o[j].x * inv, o[j].y * inv);
       pk.y = Storage<T>::pack2(o[j].z * inv, o[j].w * inv);
-      *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + row * D + 4 * c4) = pk;
+      store_out<T, GATHER>(a, sink_out<CAS, GATHER>(a, sink, h, m) + 4 * c4, pk);
     }
   }
 }
 
 // Picks the per-lane slot count for the group's nh x D outputs: 4, 8 or 16 float4 per lane
 // per chunk, with 4, 2 or 1 chunks' loads in flight (64 registers of loads in each case).
-template <typename T, int D, int HPW, bool CAS>
+template <typename T, int D, int HPW, bool CAS, bool GATHER>
 __device__ __forceinline__ void merge_chunks(const DecodeArgs& a, const Seg& s, int slots_per_chunk, int mu, int nh,
                                              const RowSink& sink, int lane) {
   constexpr int Q = D / 4;
   const int n4 = nh * Q;
   if (n4 <= 128) {
-    merge_chunks_impl<T, D, HPW, 4, 4, CAS>(a, s, slots_per_chunk, mu, nh, sink, lane);
+    merge_chunks_impl<T, D, HPW, 4, 4, CAS, GATHER>(a, s, slots_per_chunk, mu, nh, sink, lane);
   } else if (HPW * Q > 128 && n4 <= 256) {
-    merge_chunks_impl<T, D, HPW, (HPW * Q > 128 ? 8 : 4), 1, CAS>(a, s, slots_per_chunk, mu, nh, sink, lane);
+    merge_chunks_impl<T, D, HPW, (HPW * Q > 128 ? 8 : 4), 1, CAS, GATHER>(a, s, slots_per_chunk, mu, nh, sink, lane);
   } else if (HPW * Q > 256) {
-    merge_chunks_impl<T, D, HPW, (HPW * Q > 256 ? 16 : 4), 1, CAS>(a, s, slots_per_chunk, mu, nh, sink, lane);
+    merge_chunks_impl<T, D, HPW, (HPW * Q > 256 ? 16 : 4), 1, CAS, GATHER>(a, s, slots_per_chunk, mu, nh, sink, lane);
   }
 }
 
@@ -725,6 +780,39 @@ __device__ __forceinline__ void cascade_arrive(const DecodeArgs& a, const RowSin
   }
 }
 
+// End of a head-gather launch, by every consumer thread of every CTA. The CTA meets at a barrier
+// (its rows, local and over NVLink, are stored), and one thread counts the CTA with a GPU-scope
+// releasing atomic. The CTA that completes the count acquires every CTA's rows through it, fences
+// at system scope and publishes this launch's epoch in every rank's flags with system-scope
+// releases: a peer that acquires its flag sees every row this GPU stored (release and acquire are
+// cumulative along the chain barrier, GPU-scope count, system-scope flag). It then waits until
+// every rank's epoch has arrived in this rank's flags (an epoch at or past this launch's also
+// counts: a peer may already be one launch ahead), for at most kPeerWaitNs; on timeout it sets
+// kStatusPeerTimeout and leaves. It returns the count to zero for the next launch. One system-scope
+// fence per launch instead of one per thread: measured 176 against 188 us at two GPUs.
+__device__ void gather_finish(const DecodeArgs& a, int nthreads) {
+  named_barrier(15, nthreads);
+  if (threadIdx.x != 0) return;
+  const Gather& g = a.gat;
+  if (atom_add_acq_rel_gpu(g.done, 1u) != gridDim.x - 1) return;
+  fence_acq_rel_sys();
+  for (int r = 0; r < g.ranks; ++r) st_release_sys(g.flags[r] + g.rank, g.epoch);
+  const uint32_t* own = g.flags[g.rank];
+  const uint64_t t0 = globaltimer_ns();
+  bool late = false;
+  for (int r = 0; r < g.ranks && !late; ++r) {
+    while (static_cast<int32_t>(ld_acquire_sys(own + r) - g.epoch) < 0) {
+      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        atomicOr(a.sync, kStatusPeerTimeout);
+        late = true;
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  *reinterpret_cast<volatile uint32_t*>(g.done) = 0u;
+}
+
 // ------------------------------------------------------------------------- tensor-core kernel
 
 struct TcLayout {
@@ -734,8 +822,9 @@ struct TcLayout {
 __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 // groups > 0: a cascade over that many prefix groups (plan entries for prefix items as well).
-__host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int nstage, int batch, int eb = 2,
-                                              int groups = 0) {
+// streams > 1: each warp walks its own range (no combine slots).
+__host__ __device__ inline TcLayout tc_layout(int D, int NT, int TW, int streams, int nstage, int batch, int eb = 2,
+                                              int groups = 0, int HT = 1) {
   TcLayout L{};
   L.head_bytes = kTile * D * eb;  // one head's K (or V) rows of a tile (eb bytes per element)
   L.half = HT * L.head_bytes;
@@ -745,8 +834,9 @@ __host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int
   off += nstage * L.stage_bytes;
   L.bars = off;
   off += 2u * nstage * 8u;
-  // Combine slots for the warps that hand their (m, l, acc) to a tw == 0 warp: all but kCW / TW.
-  const uint32_t red_warps = TW > 1 ? kCW - kCW / TW : 0;
+  // Shared ring with TW > 1: combine slots for the warps that hand their (m, l, acc) to a tw == 0
+  // warp (all but kCW / TW). Streams need none.
+  const uint32_t red_warps = TW > 1 && streams == 1 ? kCW - kCW / TW : 0;
   L.red_m = off;
   off += red_warps * 8u * NT * 4u;
   L.red_l = off;
@@ -772,7 +862,7 @@ __host__ __device__ inline TcLayout tc_layout(int D, int NT, int HT, int TW, int
 // hl = nt*8 + 2*t4 + e and piece c, output d = 8*OW*c + OW*g + k (k < OW), the value
 // X[c*OW/2 + k/2][nt][e + 2*(k & 1)] * f[nt][e]. Rows hl >= nh are padding. A cascade member's
 // rows go to its side's fp32 state (with lse), the others to out as T.
-template <typename T, int D, int NT, int OW, bool CAS>
+template <typename T, int D, int NT, int OW, bool CAS, bool GATHER>
 __device__ __forceinline__ void store_rows(const DecodeArgs& a, const RowSink& sink, const float (&X)[D / 16][NT][4],
                                            const float (&f)[NT][2], const float (&lse)[NT][2], int g, int t4,
                                            int nh) {
@@ -800,7 +890,7 @@ __device__ __forceinline__ void store_rows(const DecodeArgs& a, const RowSink& s
         }
         if (g == 0) a.cas_lse[srow] = lse[nt][e];
       } else {
-        T* orow = static_cast<T*>(a.out) + row * D;
+        const int64_t orow = sink_out<CAS, GATHER>(a, sink, hl, m);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
 #pragma unroll
@@ -811,7 +901,7 @@ __device__ __forceinline__ void store_rows(const DecodeArgs& a, const RowSink& s
             pk.y = Storage<T>::pack2(X[m0 + 1][nt][e] * x, X[m0 + 1][nt][e + 2] * x);
             pk.z = Storage<T>::pack2(X[m0 + 2][nt][e] * x, X[m0 + 2][nt][e + 2] * x);
             pk.w = Storage<T>::pack2(X[m0 + 3][nt][e] * x, X[m0 + 3][nt][e + 2] * x);
-            *reinterpret_cast<uint4*>(orow + c * 8 * OW + OW * g + 8 * h) = pk;
+            store_out<T, GATHER>(a, orow + c * 8 * OW + OW * g + 8 * h, pk);
           }
         }
       }
@@ -819,10 +909,10 @@ __device__ __forceinline__ void store_rows(const DecodeArgs& a, const RowSink& s
   }
 }
 
-template <typename T, int D, int NT, bool KV8, bool CAS>
+template <typename T, int D, int NT, bool KV8, bool CAS, bool GATHER>
 __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                                   const __grid_constant__ CUtensorMap tmv,
-                                                                  const DecodeArgs a, const TcShape cfg) {
+                                                                  const __grid_constant__ DecodeArgs a, const TcShape cfg) {
   // KV8: the cache holds e4m3 (one byte per element, per-KV-head scales) and the MMAs run in
   // f16 (e4m3 converts to f16 exactly); otherwise the cache and the MMAs use T.
   using MT = typename std::conditional<KV8, __half, T>::type;
@@ -835,7 +925,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int HT = cfg.ht, HG = cfg.hg, TW = cfg.tw, nstage = cfg.nstage;
-  const TcLayout L = tc_layout(D, NT, HT, TW, nstage, a.batch, EB, a.num_prefixes);
+  const TcLayout L = tc_layout(D, NT, TW, cfg.ns, nstage, a.batch, EB, a.num_prefixes, HT);
   const uint32_t ring = smem_u32(smem + L.ring);
   const uint32_t bars = smem_u32(smem + L.bars);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m);
@@ -856,10 +946,20 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  // Streams: when a tile holds one (head, group) pair (HT * HG == 1, TW == 8), warp t is stream t:
+  // it walks its own range of the plan (range CTA * TW + t) and reads its own ring stages t,
+  // t + TW, t + 2 TW, ... (SPS of them); no warp waits for another, and the producer feeds every
+  // stream. Otherwise (NS == 1) the CTA has one range and one ring: the HT * HG warps of a tile
+  // read every stage, and with TW > 1 the TW warps of a (head, group) take its tiles in turn and
+  // combine at the end of a segment. Streams measured 205.5 -> 186.2 us at 512 sequences x 4096
+  // tokens of one KV head (Llama-3-8B heads sharded 8 ways), and slower than the shared ring with
+  // two or four warps a stream (their ranges cut the plan 2-4 times finer: more split merges).
+  const int NS = NT == 1 ? cfg.ns : 1;  // streams (ranges) of this CTA
+  const int SPS = nstage / NS;             // stages per stream (nstage is a multiple of TW)
   if (threadIdx.x == 0) {
     for (int s = 0; s < nstage; ++s) {
       mbar_init(bars + 8u * s, 1);                   // full: the producer's expect_tx arrival
-      mbar_init(bars + 8u * (nstage + s), HT * HG);  // empty: every warp that reads the stage
+      mbar_init(bars + 8u * (nstage + s), HT * HG);  // empty: every warp of the stream reads the stage
     }
     fence_barrier_init();
   }
@@ -873,7 +973,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   // CTAs can only take an SM this grid has left.
   wait_prior_grid();
   allow_next_grid();
-  plan_build(a, ps);
+  plan_build(a, ps, NS);
   volatile int* abort_flag = misc + 2;
 
   if (warp == kCW) {
@@ -895,6 +995,102 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     const int p_rows = cfg.p_rows;
     const int nsub = kTile / p_rows;
     const uint32_t sub_bytes = 2u * p_rows * rows_per_tok * 128u;
+    if (NT == 1 && NS > 1) {
+      // Stream mode: lane t < NS feeds stream t. It walks the stream's range, looks each tile's
+      // page(s) up one tile ahead (a plain load whose latency hides behind the stream's stages) and
+      // issues the tile as soon as the stream's next stage is free; no lane waits for another, so a
+      // stream whose warps are busy with a segment's end holds back only its own stages.
+      const bool mine = lane < NS;
+      Walk sw;
+      Seg ss;
+      if (mine) walk_init(a, misc, sw, static_cast<int>(blockIdx.x) * NS + lane, static_cast<int>(gridDim.x) * NS);
+      bool done = !mine, live = false;
+      int j = 0, ntiles = 0, piece0 = 0;
+      uint32_t k = 0;  // tiles issued on this stream
+      const int32_t* bt_row = nullptr;
+      uint64_t policy = policy_stream;
+      bool pv[2] = {false, false};
+      int py[2] = {0, 0};
+      auto lookup = [&](int jj) {  // tile jj's page pieces: TMA row coordinate, or invalid
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int tok = ss.tok_begin + jj * kTile + r * p_rows;
+          pv[r] = false;
+          py[r] = 0;
+          if (r < nsub && tok < ss.tok_end) {
+            const int pidx = tok / a.page_size;
+            const int page = __ldg(bt_row + pidx);
+            const bool good = page >= 0 && (a.num_pages < 0 || page < a.num_pages);
+            if (!good) atomicOr(a.sync, kStatusBadPage);
+            pv[r] = good;
+            py[r] = good ? page * a.page_size + (tok - pidx * a.page_size) : 0;
+          }
+        }
+      };
+      uint64_t idle_since = clock64();
+      while (__any_sync(0xffffffffu, !done)) {
+        if (*abort_flag) break;
+        bool progressed = false;
+        if (!done && !live) {
+          bool got = walk_next<CAS>(a, ps, sw, ss);
+          while (got && ss.tok_end <= ss.tok_begin) got = walk_next<CAS>(a, ps, sw, ss);  // empty splits
+          if (!got) {
+            done = true;
+          } else {
+            live = true;
+            j = 0;
+            ntiles = (ss.tok_end - ss.tok_begin + kTile - 1) / kTile;
+            const bool shared = CAS && ss.grp >= 0;
+            bt_row = shared ? a.prefix_bt + static_cast<int64_t>(ss.grp) * a.prefix_bt_stride
+                            : a.block_table + static_cast<int64_t>(ss.seq) * a.bt_stride;
+            policy = shared ? policy_shared : policy_stream;
+            piece0 = ss.u * rows_per_tok;
+            lookup(0);
+          }
+        }
+        if (live) {
+          const uint32_t stage = static_cast<uint32_t>(lane) + NS * (k % SPS);
+          if (mbar_test_wait(bars + 8u * (nstage + stage), ((k / SPS) & 1u) ^ 1u)) {
+            const uint32_t full = bars + 8u * stage;
+            mbar_arrive_expect_tx(full, (pv[0] ? sub_bytes : 0u) + (pv[1] ? sub_bytes : 0u));
+            const uint32_t sbase = ring + stage * L.stage_bytes;
+            if (pv[0]) {
+              tma_load_3d(sbase, &tmk, 0, piece0, py[0], full, policy);
+              tma_load_3d(sbase + L.half, &tmv, 0, piece0, py[0], full, policy);
+            }
+            if (pv[1]) {
+              const uint32_t off = p_rows * rows_per_tok * 128u;
+              tma_load_3d(sbase + off, &tmk, 0, piece0, py[1], full, policy);
+              tma_load_3d(sbase + L.half + off, &tmv, 0, piece0, py[1], full, policy);
+            }
+            ++k;
+            progressed = true;
+            if (++j < ntiles) {
+              lookup(j);
+            } else {
+              live = false;
+            }
+          }
+        }
+        if (__any_sync(0xffffffffu, progressed)) {
+          idle_since = clock64();
+        } else {
+          if (static_cast<uint64_t>(clock64()) - idle_since > kWaitLimit) {
+            if (lane == 0) atomicOr(a.sync, kStatusWaitTimeout);
+            *abort_flag = 1;
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      // Let every copy this stream issued land before the CTA may exit.
+      if (mine) {
+        for (uint32_t kk = k > static_cast<uint32_t>(SPS) ? k - SPS : 0u; kk < k; ++kk) {
+          mbar_wait_bounded(bars + 8u * (lane + NS * (kk % SPS)), (kk / SPS) & 1u, a.sync, kWaitLimit);
+        }
+      }
+      return;
+    }
     // Batched issue pays off for stages up to 32 KB (4 heads or fewer per tile); with 64 KB
     // stages a tile takes longer to arrive than a producer pass, and single-tile passes
     // measured faster (batch 256 x 8192 tokens, 70B heads).
@@ -1007,7 +1203,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   // the V loads 4-way shared-memory bank conflicts (every token of a (head, piece) has the
   // same swizzle phase); a piece-major stage with permuted token rows removes them but measured
   // no faster, the kernel being bound by HBM, not shared memory.
-  zero_empty_sequences<T>(a, ps.lens + misc[kMiscV], ps.hp, threadIdx.x, kCW * 32);
+  zero_empty_sequences<T, GATHER>(a, ps.lens + misc[kMiscV], ps.hp, threadIdx.x, kCW * 32);
   const int ht = warp % HT;
   const int hg = (warp / HT) % HG;
   const int tw = warp / (HT * HG);
@@ -1016,10 +1212,14 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   const float sl = a.scale_log2;
   const int G = a.group;
 
+  // A stream walks range CTA * NS + tw and takes every tile of its segments; in the shared ring the
+  // TW warps of a (head, group) take tiles tw, tw + TW, ... of the CTA's segments.
+  const int st = NS > 1 ? tw : 0;
+  const int j_first = NS > 1 ? 0 : tw, j_step = NS > 1 ? 1 : TW;
   Walk w;
-  walk_init(a, misc, w);
+  walk_init(a, misc, w, static_cast<int>(blockIdx.x) * NS + st, static_cast<int>(gridDim.x) * NS);
   Seg s;
-  uint32_t gt = 0;
+  uint32_t gt = 0;  // tiles of this ring (the stream's, or the CTA's) before the segment
   while (walk_next<CAS>(a, ps, w, s)) {
     const int ntok = max(0, s.tok_end - s.tok_begin);
     const int ntiles = (ntok + kTile - 1) / kTile;
@@ -1029,7 +1229,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     // latency hides behind this segment's tiles. If all of them have, this chunk is the last
     // one and merges straight from its registers at the end of the segment.
     uint32_t published = 0;
-    if (!s.whole && tw == 0 && lane == 0) published = ld_relaxed_gpu(counter_of(a, s.cb, kvh, hg));
+    if (!s.whole && (NS > 1 || tw == 0) && lane == 0) published = ld_relaxed_gpu(counter_of(a, s.cb, kvh, hg));
 
     // Q^T as the B operand, in the permuted contraction order of the K loads: one 16-byte load
     // per 32 d (16-bit cache) or two per 64 d (e4m3 cache, converted to f16).
@@ -1080,11 +1280,11 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       for (int mt = 0; mt < KS; ++mt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.0f;
     }
 
-    for (int j = tw; j < ntiles; j += TW) {
+    for (int j = j_first; j < ntiles; j += j_step) {
       const uint32_t gj = gt + j;
-      const int stage = static_cast<int>(gj % nstage);
+      const int stage = st + NS * static_cast<int>(gj % SPS);
       if (*abort_flag) break;
-      if (!mbar_wait_bounded(bars + 8u * stage, (gj / nstage) & 1u, a.sync, kWaitLimit)) {
+      if (!mbar_wait_bounded(bars + 8u * stage, (gj / SPS) & 1u, a.sync, kWaitLimit)) {
         *abort_flag = 1;
         break;
       }
@@ -1261,8 +1461,9 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
 
     // Lane (g, t4) owns, for head hl = nt*8 + 2*t4 + e and piece c, output d = 8*OW*c + OW*g + k,
     // k = 0..OW-1, held in acc[c*OW/2 + k/2][nt][e + 2*(k & 1)].
-    // Warps that split the tiles of one (head, group) combine into the tw == 0 warp.
-    if (TW > 1) {
+    // Shared ring with TW > 1: the warps that split the tiles of one (head, group) combine into
+    // the tw == 0 warp.
+    if (NS == 1 && TW > 1) {
       if (tw != 0) {
         const int slot_w = warp - HT * HG;  // warps with tw >= 1, in order
         float* rm = red_m + slot_w * HPW;
@@ -1354,7 +1555,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           lse[nt][e] = l > 0.0f ? m_run[nt][e] + __log2f(l) : -INFINITY;
         }
       }
-      store_rows<T, D, NT, OW, CAS>(a, sink, acc, inv, lse, g, t4, nh_warp);
+      store_rows<T, D, NT, OW, CAS, GATHER>(a, sink, acc, inv, lse, g, t4, nh_warp);
       if (CAS && sink.cas != 0u) cascade_arrive<T, D>(a, sink, hg, hg * HPW, nh_member, lane);
       continue;
     }
@@ -1416,7 +1617,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
     }
     __syncwarp();
     if (flat) {
-      merge_chunks<T, D, HPW, CAS>(a, s, HT * HG, mu, nh_warp, sink, lane);
+      merge_chunks<T, D, HPW, CAS, GATHER>(a, s, HT * HG, mu, nh_warp, sink, lane);
     } else {
       // Merge in chunk order with a running max, this chunk's own term from its registers (the
       // values it would have stored), so the result does not depend on which chunk merges; a
@@ -1492,13 +1693,14 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
           lse[nt][e] = wsum > 0.0f ? m_acc[nt][e] + __log2f(wsum) : -INFINITY;
         }
       }
-      store_rows<T, D, NT, OW, CAS>(a, sink, o_acc, inv, lse, g, t4, nh_warp);
+      store_rows<T, D, NT, OW, CAS, GATHER>(a, sink, o_acc, inv, lse, g, t4, nh_warp);
     }
     if (CAS && sink.cas != 0u) cascade_arrive<T, D>(a, sink, hg, hg * HPW, nh_member, lane);
     // Every sibling has counted (or none needed to): nobody else touches the counter in this
     // launch, so a plain store returns it to zero for the next one.
     if (lane == 0) *reinterpret_cast<volatile uint32_t*>(counter) = 0u;
   }
+  if constexpr (GATHER) gather_finish(a, kCW * 32);
 }
 
 // ------------------------------------------------------------------------- tensor-core prefix kernel
@@ -1566,7 +1768,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmq,
                                                                            const __grid_constant__ CUtensorMap tmk,
                                                                            const __grid_constant__ CUtensorMap tmv,
-                                                                           const DecodeArgs a) {
+                                                                           const __grid_constant__ DecodeArgs a) {
   constexpr int CT = kPrefixTokens;
   constexpr int NH = D / 64;                  // 128-byte column blocks of a head row
   constexpr uint32_t QH = 128u * 128u;        // one column block of Q: 128 rows
@@ -1732,14 +1934,20 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
   const float sl = a.scale_log2;
   float m_used = -INFINITY, lsum = 0.0f;
   bool ok = true;
+  int j_last = 0;  // the last chunk whose loads were issued and waited for
+  // A wait that runs out (thread 0's Q or K, anyone's S, V or O) flags the launch. Every copy
+  // already issued is still waited for (bounded) before the CTA may leave: no wait is skipped
+  // after a failure, thread 0 issues no further chunk once one of its waits failed, and the CTA
+  // leaves the loop, by one verdict, after that chunk's V has landed.
 #pragma unroll 1
   for (int j = 0; j < nchunk; ++j) {
     const int s = j & 1;
     const int ntok = min(CT, seg_tokens - j * CT);
+    j_last = j;
     if (tid == 0) {
-      bool got = j > 0 || mbar_wait_bounded(bq, 0, a.sync, kWaitLimit);
-      got = got && mbar_wait_bounded(bk(s), (j >> 1) & 1, a.sync, kWaitLimit);
-      ok = ok && got;
+      const bool gq = j > 0 || mbar_wait_bounded(bq, 0, a.sync, kWaitLimit);
+      const bool gk = mbar_wait_bounded(bk(s), (j >> 1) & 1, a.sync, kWaitLimit);
+      ok = ok && gq && gk;
       if (ok) {
         tcgen05_fence_after();
 #pragma unroll
@@ -1756,7 +1964,10 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     // S of chunk j implies; warp 0 then starts chunk j + 1's loads.
     ok = mbar_wait_bounded(bs, j & 1, a.sync, kWaitLimit) && ok;
     tcgen05_fence_after();
-    if (warp == 0 && j + 1 < nchunk) issue_chunk(j + 1);
+    if (warp == 0) {
+      const bool lead_ok = __shfl_sync(0xffffffffu, ok, 0);  // thread 0's waits so far
+      if (j + 1 < nchunk && lead_ok) issue_chunk(j + 1);
+    }
 
     // ---- this thread's half row of S: the chunk's maximum, a lazy rescale, P
     uint32_t sr[SC / 32][32];
@@ -1781,7 +1992,8 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
     };
     float mc = full ? half_max(std::true_type{}) : half_max(std::false_type{});
     s_half[hf * 128 + rw] = mc;
-    __syncthreads();
+    // One verdict for the CTA: thread 0's ok is the one warp 0 used to decide on chunk j + 1.
+    const bool stop = __syncthreads_or(tid == 0 && !ok);
     mc = fmaxf(s_half[rw], s_half[128 + rw]);
     float alpha = 1.0f;
     if (mc > m_used + kLazyRescale) {  // also the first chunk, where m_used = -inf
@@ -1855,8 +2067,9 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
       }
       umma_commit(bo);
     }
+    if (stop) break;  // chunk j + 1 was not issued
   }
-  ok = mbar_wait_bounded(bo, (nchunk - 1) & 1, a.sync, kWaitLimit) && ok;
+  ok = mbar_wait_bounded(bo, j_last & 1, a.sync, kWaitLimit) && ok;
   s_half[hf * 128 + rw] = lsum;
   ok = __syncthreads_and(ok);  // one verdict for the CTA (only thread 0 waited on the loads)
   lsum = s_half[rw] + s_half[128 + rw];  // the two halves' sums, in a fixed order
@@ -1921,7 +2134,7 @@ __global__ void __launch_bounds__(kPrefixThreads, 1) cascade_prefix_kernel(const
 constexpr int kReduceThreads = 256;
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kReduceThreads) cascade_prefix_reduce_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kReduceThreads) cascade_prefix_reduce_kernel(const __grid_constant__ DecodeArgs a) {
   constexpr int Q = D / 4;
   static_assert(32 % Q == 0, "a query row's columns must sit in one warp");
   constexpr int KB = 8;
@@ -2014,7 +2227,7 @@ __host__ __device__ inline GenLayout gen_layout(int G, int D, int batch) {
 
 // One CTA of 128 threads handles one (sequence, KV head) chunk at a time.
 template <typename T>
-__global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(16) uint8_t gsmem[];
   const int G = a.group, D = a.head_dim, H = a.num_kv_heads;
   const GenLayout L = gen_layout(G, D, a.batch);
@@ -2035,7 +2248,7 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const Decod
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   plan_build(a, ps);
-  zero_empty_sequences<T>(a, ps.lens, nullptr, tid, kGenThreads);
+  zero_empty_sequences<T, false>(a, ps.lens, nullptr, tid, kGenThreads);
   const int64_t tok_stride = static_cast<int64_t>(H) * D;
   T* out = static_cast<T*>(a.out);
 
@@ -2186,6 +2399,7 @@ struct Plan {
   int min_tiles = kMinTilesPerCta;
   bool kv8 = false;
   int groups = 0;   // cascade: prefix groups (0: plain decode)
+  bool gather = false;  // the kernel stores its rows into other GPUs' outputs too
   int members = 1;  // cascade: sequences packed into one prefix item
   int prefix_chunk = 0;  // cascade: tokens per tensor-core prefix chunk (0: prefix items in the plan)
   int cas_planes = 1;    // cascade: prefix planes per sequence (chunks of the longest prefix)
@@ -2240,20 +2454,28 @@ int blocks_per_sm(int dev, const void* fn, int threads, size_t smem) {
   return n;
 }
 
+// Every tensor-core kernel instantiation has this signature.
+using TcKernel = void (*)(CUtensorMap, CUtensorMap, DecodeArgs, TcShape);
+
+// The instantiation for a plan: cascades have no gather, and the gather exists for 16-bit caches only.
 template <typename T, int D, int NT, bool KV8>
-const void* tc_fn_one(bool cas) {
-  return cas ? (const void*)decode_tc_kernel<T, D, NT, KV8, true> : (const void*)decode_tc_kernel<T, D, NT, KV8, false>;
+TcKernel tc_kernel_one(bool cas, bool gather) {
+  if (cas) return decode_tc_kernel<T, D, NT, KV8, true, false>;
+  if constexpr (!KV8) {
+    if (gather) return decode_tc_kernel<T, D, NT, false, false, true>;
+  }
+  return decode_tc_kernel<T, D, NT, KV8, false, false>;
 }
 
 template <typename T>
-const void* tc_fn(int D, int NT, bool kv8, bool cas) {
+TcKernel tc_kernel(int D, int NT, bool kv8, bool cas, bool gather) {
   if (kv8) {
-    if (D == 128) return NT == 1 ? tc_fn_one<T, 128, 1, true>(cas) : tc_fn_one<T, 128, 2, true>(cas);
-    return tc_fn_one<T, 256, 1, true>(cas);
+    if (D == 128) return NT == 1 ? tc_kernel_one<T, 128, 1, true>(cas, false) : tc_kernel_one<T, 128, 2, true>(cas, false);
+    return tc_kernel_one<T, 256, 1, true>(cas, false);
   }
-  if (D == 64) return NT == 1 ? tc_fn_one<T, 64, 1, false>(cas) : tc_fn_one<T, 64, 2, false>(cas);
-  if (D == 128) return NT == 1 ? tc_fn_one<T, 128, 1, false>(cas) : tc_fn_one<T, 128, 2, false>(cas);
-  return tc_fn_one<T, 256, 1, false>(cas);
+  if (D == 64) return NT == 1 ? tc_kernel_one<T, 64, 1, false>(cas, gather) : tc_kernel_one<T, 64, 2, false>(cas, gather);
+  if (D == 128) return NT == 1 ? tc_kernel_one<T, 128, 1, false>(cas, gather) : tc_kernel_one<T, 128, 2, false>(cas, gather);
+  return tc_kernel_one<T, 256, 1, false>(cas, gather);
 }
 
 const void* gen_fn(int dtype) {
@@ -2291,7 +2513,7 @@ size_t lse_offset(int slots, int slot_heads, int D) {
 // groups > 0: a cascade over that many shared-prefix groups of at most prefix_max_pages pages
 // (tensor-core kernel and balanced plan only).
 int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages, int num_splits, bool generic,
-              Plan& p, bool kv8 = false, int groups = 0, int prefix_max_pages = 0) {
+              Plan& p, bool kv8 = false, int groups = 0, int prefix_max_pages = 0, bool gather = false) {
   if (batch <= 0 || batch > kMaxBatch || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || D <= 0 || P <= 0 ||
       max_pages < 0 || num_splits < 0 || groups < 0 || groups > kMaxBatch || prefix_max_pages < 0) {
     return static_cast<int>(cudaErrorInvalidValue);
@@ -2373,21 +2595,37 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     p.shape.hg = HG;
     p.shape.tw = kCW / (ht * HG);
     p.shape.p_rows = P < 16 ? P : 16;
-    const TcLayout base = tc_layout(D, NT, ht, p.shape.tw, 0, batch, eb, groups);
-    const uint32_t stage = base.stage_bytes + 16u;
-    int ns = base.total < kTcSmemBudget ? static_cast<int>((kTcSmemBudget - base.total) / stage) : 0;
-    ns = std::min(kMaxStages, ns);
+    // Streams (one warp a stream) when a tile holds one (head, group) pair, the kernel has one
+    // n-tile (the two-n-tile kernels have no registers to spare for the stream producer) and the
+    // ring holds at least two stages a stream; otherwise one shared ring.
     const int forced_ns = env_int("KL_DECODE_STAGES");
-    if (forced_ns >= 2) ns = std::min(ns, forced_ns);
-    // Stage s is consumed only by the warps with tw == s % TW, in order, so a warp never
-    // waits on a stage whose previous phase belongs to another warp: with a stage count
-    // that is not a multiple of TW, a wait for phase k could be satisfied by phase k-2
-    // (same parity) and the ring would fall out of step.
-    ns = ns / p.shape.tw * p.shape.tw;
-    if (ns < std::max(2, p.shape.tw)) return static_cast<int>(cudaErrorInvalidValue);
+    auto ring_stages = [&](int streams) {
+      const TcLayout base = tc_layout(D, NT, p.shape.tw, streams, 0, batch, eb, groups, ht);
+      const uint32_t stage = base.stage_bytes + 16u;
+      int n = base.total < kTcSmemBudget ? static_cast<int>((kTcSmemBudget - base.total) / stage) : 0;
+      n = std::min(kMaxStages, n);
+      if (forced_ns >= 2) n = std::min(n, forced_ns);
+      return n / p.shape.tw * p.shape.tw;
+    };
+    int streams = ht * HG == 1 && NT == 1 ? p.shape.tw : 1;
+    int ns = ring_stages(streams);
+    if (streams > 1 && ns < 2 * streams) {
+      streams = 1;
+      ns = ring_stages(1);
+    }
+    // The stage count is a multiple of TW. Streams: stream t owns stages t, t + TW, ..., at least
+    // two. Shared ring: stage s is consumed only by the warps with tw == s % TW, in order, so a
+    // warp never waits on a stage whose previous phase belongs to another warp (with a stage
+    // count that is not a multiple of TW, a wait for phase k could be satisfied by phase k-2, of
+    // the same parity, and the ring would fall out of step).
+    if (ns < std::max(2, p.shape.tw) || ns < 2 * streams) return static_cast<int>(cudaErrorInvalidValue);
     p.shape.nstage = ns;
-    p.smem = tc_layout(D, NT, ht, p.shape.tw, ns, batch, eb, groups).total;
-    p.fn = dtype == KL_FLOAT16 ? tc_fn<__half>(D, NT, kv8, cascade) : tc_fn<__nv_bfloat16>(D, NT, kv8, cascade);
+    p.shape.ns = streams;
+    p.smem = tc_layout(D, NT, p.shape.tw, streams, ns, batch, eb, groups, ht).total;
+    p.fn = reinterpret_cast<const void*>(
+        dtype == KL_FLOAT16 ? tc_kernel<__half>(D, NT, kv8, cascade, gather)
+                            : tc_kernel<__nv_bfloat16>(D, NT, kv8, cascade, gather));
+    p.gather = gather;
     p.units = Hkv / ht;
     p.slot_heads = 8 * NT;
     p.groups = groups;
@@ -2415,11 +2653,14 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
     p.pps = (mp + num_splits - 1) / num_splits;
     p.splits = (mp + p.pps - 1) / p.pps;
     chunks = static_cast<int64_t>(batch) * p.units * p.splits;
-    p.grid = static_cast<int>(std::min<int64_t>(chunks, static_cast<int64_t>(sms) * per_sm));
+    // Every stream of a CTA walks its own items.
+    const int streams = p.tc ? p.shape.ns : 1;
+    p.grid = static_cast<int>(std::min<int64_t>((chunks + streams - 1) / streams, static_cast<int64_t>(sms) * per_sm));
   } else {
     p.splits = 0;
     p.grid = sms * per_sm;
-    chunks = 2LL * p.grid;
+    // Two chunk ids per range: the plan is cut into grid * streams ranges.
+    chunks = 2LL * p.grid * (p.tc ? p.shape.ns : 1);
   }
   if (chunks * slots_per_chunk > INT_MAX / 2) return static_cast<int>(cudaErrorInvalidValue);
   const int forced_min = env_int("KL_DECODE_MIN_TILES");
@@ -2524,33 +2765,12 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, int threads, size_t
   return launch_kernel(decode_pdl(), kernel, grid, dim3(static_cast<unsigned>(threads)), smem, st, args...);
 }
 
-template <typename T, int D, int NT, bool KV8>
-cudaError_t launch_tc_one(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                          cudaStream_t st) {
-  // The kernel's prologue may overlap the previous kernel in the stream (see decode_tc_kernel).
-  const dim3 grid(static_cast<unsigned>(p.grid));
-  if (p.groups > 0) return launch_pdl(decode_tc_kernel<T, D, NT, KV8, true>, grid, kTCThreads, p.smem, st, tmk, tmv, a, p.shape);
-  return launch_pdl(decode_tc_kernel<T, D, NT, KV8, false>, grid, kTCThreads, p.smem, st, tmk, tmv, a, p.shape);
-}
-
-template <typename T, bool KV8>
-cudaError_t launch_tc_kind(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                           cudaStream_t st) {
-  if constexpr (!KV8) {
-    if (p.D == 64) {
-      return p.NT == 1 ? launch_tc_one<T, 64, 1, false>(p, tmk, tmv, a, st) : launch_tc_one<T, 64, 2, false>(p, tmk, tmv, a, st);
-    }
-  }
-  if (p.D == 128) {
-    return p.NT == 1 ? launch_tc_one<T, 128, 1, KV8>(p, tmk, tmv, a, st) : launch_tc_one<T, 128, 2, KV8>(p, tmk, tmv, a, st);
-  }
-  return launch_tc_one<T, 256, 1, KV8>(p, tmk, tmv, a, st);
-}
-
-template <typename T>
+// The plan's kernel instantiation (p.fn), launched with programmatic stream serialization: its
+// prologue may overlap the previous kernel in the stream (see decode_tc_kernel).
 cudaError_t launch_tc(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                       cudaStream_t st) {
-  return p.kv8 ? launch_tc_kind<T, true>(p, tmk, tmv, a, st) : launch_tc_kind<T, false>(p, tmk, tmv, a, st);
+  const TcKernel kernel = reinterpret_cast<TcKernel>(const_cast<void*>(p.fn));
+  return launch_pdl(kernel, dim3(static_cast<unsigned>(p.grid)), kTCThreads, p.smem, st, tmk, tmv, a, p.shape);
 }
 
 // The kernel one call takes, and its plan: the tensor-core kernel where the shape allows it, the
@@ -2561,10 +2781,11 @@ cudaError_t launch_tc(const Plan& p, const CUtensorMap& tmk, const CUtensorMap& 
 // point that launches a decode, or sizes scratch for one it will launch, decides here.
 int choose_kernel(int dtype, const void* out, const void* q, const void* k_cache, const void* v_cache, int batch,
                   int Hq, int Hkv, int D, int P, int max_pages, int64_t num_pages, int num_splits, bool kv8,
-                  const CascadeIn& cas, Plan& p, CUtensorMap* tmk, CUtensorMap* tmv, bool* use_tc) {
+                  const CascadeIn& cas, Plan& p, CUtensorMap* tmk, CUtensorMap* tmv, bool* use_tc,
+                  bool gather = false) {
   *use_tc = false;
   if (const int rc = make_plan(dtype, batch, Hq, Hkv, D, P, max_pages, num_splits, false, p, kv8, cas.groups,
-                               cas.max_pages)) {
+                               cas.max_pages, gather)) {
     return rc;
   }
   const bool tc_ok = p.tc && aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(q, 16) && aligned(out, 16) &&
@@ -2584,7 +2805,8 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
                 const int32_t* block_table, const int32_t* seq_lens, int batch, int Hq, int Hkv, int D, int P,
                 int64_t bt_stride, int max_pages, int64_t num_pages, float scale, int num_splits, void* partials,
                 size_t partial_bytes, void* sync, size_t sync_bytes, cudaStream_t st,
-                const float* k_scale = nullptr, const float* v_scale = nullptr, const CascadeIn& cas = CascadeIn{}) {
+                const float* k_scale = nullptr, const float* v_scale = nullptr, const CascadeIn& cas = CascadeIn{},
+                const kl_head_gather_t* gather = nullptr) {
   if (batch == 0) return 0;
   if (!out || !q || !k_cache || !v_cache || !block_table || !seq_lens || !sync) {
     return static_cast<int>(cudaErrorInvalidValue);
@@ -2597,18 +2819,39 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   const bool kv8 = k_scale != nullptr || v_scale != nullptr;
   if (kv8 && (!k_scale || !v_scale)) return static_cast<int>(cudaErrorInvalidValue);
   if (bt_stride < 0 || (batch > 1 && bt_stride < max_pages)) return static_cast<int>(cudaErrorInvalidValue);
+  // A head gather runs on the tensor-core kernel of plain decode only.
+  const bool gathering = gather != nullptr && gather->num_ranks > 1;
   Plan p;
   CUtensorMap tmk, tmv;
   bool use_tc = false;
   if (const int rc = choose_kernel(dtype, out, q, k_cache, v_cache, batch, Hq, Hkv, D, P, max_pages, num_pages,
-                                   num_splits, kv8, cas, p, &tmk, &tmv, &use_tc)) {
+                                   num_splits, kv8, cas, p, &tmk, &tmv, &use_tc, gathering && !cascade && !kv8)) {
     return rc;
   }
   if (partial_bytes < p.part_bytes || sync_bytes < p.sync_bytes || !partials) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
+  if (gathering && (!use_tc || cascade || kv8 || !p.gather)) return static_cast<int>(cudaErrorNotSupported);
   DecodeArgs a{};
   a.out = out;
+  a.out_seq_stride = static_cast<int64_t>(Hq) * D;
+  if (gather != nullptr) {
+    // This rank's heads [rank * Hq, (rank + 1) * Hq) of every rank's [batch, ranks * Hq, D] output.
+    const size_t eb = dtype == KL_FLOAT32 ? 4 : 2;
+    const size_t head_off = static_cast<size_t>(gather->rank) * Hq * D * eb;
+    a.out_seq_stride = static_cast<int64_t>(gather->num_ranks) * Hq * D;
+    a.out = static_cast<uint8_t*>(gather->out[gather->rank]) + head_off;
+    if (gathering) {
+      a.gat.ranks = gather->num_ranks;
+      a.gat.rank = gather->rank;
+      a.gat.epoch = gather->epoch;
+      a.gat.done = gather->done;
+      for (int r = 0; r < gather->num_ranks; ++r) {
+        a.gat.out[r] = static_cast<uint8_t*>(gather->out[r]) + head_off;
+        a.gat.flags[r] = gather->flags[r];
+      }
+    }
+  }
   a.q = q;
   a.k_cache = k_cache;
   a.v_cache = v_cache;
@@ -2685,8 +2928,7 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
   }
 
   if (use_tc) {
-    const cudaError_t e = dtype == KL_FLOAT16 ? launch_tc<__half>(p, tmk, tmv, a, st)
-                                              : launch_tc<__nv_bfloat16>(p, tmk, tmv, a, st);
+    const cudaError_t e = launch_tc(p, tmk, tmv, a, st);
     return static_cast<int>(e);
   }
   switch (dtype) {
@@ -2823,6 +3065,57 @@ int kl_paged_decode_attention(int dtype, void* out, const void* q, const void* k
   const cudaError_t f = cudaFreeAsync(buf, st);
   return rc != 0 ? rc : static_cast<int>(f);
 }
+
+int kl_paged_decode_gather(int dtype, const kl_head_gather_t* gather, const void* q, const void* k_cache,
+                           const void* v_cache, const int32_t* block_table, const int32_t* seq_lens, int batch,
+                           int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                           int64_t block_table_stride, int max_pages_per_seq, int64_t num_pages, float scale,
+                           void* partials, size_t partial_bytes, void* sync, size_t sync_bytes, void* stream) {
+  if (!gather || gather->num_ranks < 1 || gather->num_ranks > KL_GATHER_MAX_RANKS || gather->rank < 0 ||
+      gather->rank >= gather->num_ranks) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  for (int r = 0; r < gather->num_ranks; ++r) {
+    if (!gather->out[r] || (gather->num_ranks > 1 && !gather->flags[r])) return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (gather->num_ranks > 1 && (!gather->done || gather->epoch == 0u)) return static_cast<int>(cudaErrorInvalidValue);
+  if (batch == 0) return 0;
+  return klb::decode_impl(dtype, gather->out[gather->rank], q, k_cache, v_cache, block_table, seq_lens, batch,
+                          num_q_heads, num_kv_heads, head_dim, page_size, block_table_stride, max_pages_per_seq,
+                          num_pages, scale, 0, partials, partial_bytes, sync, sync_bytes,
+                          static_cast<cudaStream_t>(stream), nullptr, nullptr, klb::CascadeIn{}, gather);
+}
+
+int kl_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return static_cast<int>(cudaErrorInvalidValue);
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h{};
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return static_cast<int>(e);
+  }
+  static_assert(sizeof(h) == KL_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return 0;
+}
+
+int kl_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return static_cast<int>(cudaErrorInvalidValue);
+  cudaIpcMemHandle_t h{};
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  return static_cast<int>(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int kl_ipc_close(void* ptr) { return ptr ? static_cast<int>(cudaIpcCloseMemHandle(ptr)) : 0; }
+
+int kl_ipc_free(void* ptr) { return ptr ? static_cast<int>(cudaFree(ptr)) : 0; }
 
 int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* stream) {
   if (!sync || !status) return static_cast<int>(cudaErrorInvalidValue);

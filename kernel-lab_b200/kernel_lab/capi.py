@@ -74,7 +74,33 @@ SIGNATURES = {
          _c_i64, _c_float, _c_int, _c_vp],
     ),
     "kl_paged_decode_noalloc_read_status": (_c_int, [_c_u32p, _c_int, _c_vp]),
+    "kl_paged_decode_gather": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_int,
+         _c_i64, _c_float, _c_vp, _c_sz, _c_vp, _c_sz, _c_vp],
+    ),
+    "kl_ipc_alloc": (_c_int, [_c_sz, ctypes.POINTER(_c_vp), _c_vp]),
+    "kl_ipc_open": (_c_int, [_c_vp, ctypes.POINTER(_c_vp)]),
+    "kl_ipc_close": (_c_int, [_c_vp]),
+    "kl_ipc_free": (_c_int, [_c_vp]),
 }
+
+KL_STATUS_PEER_TIMEOUT = 16
+KL_GATHER_MAX_RANKS = 8
+KL_IPC_HANDLE_BYTES = 64
+
+
+class HeadGather(ctypes.Structure):
+    """kl_head_gather_t: one call's head gather (ranks, epoch, every rank's output and flags)."""
+
+    _fields_ = [
+        ("num_ranks", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("epoch", ctypes.c_uint32),
+        ("out", ctypes.c_void_p * KL_GATHER_MAX_RANKS),
+        ("flags", ctypes.c_void_p * KL_GATHER_MAX_RANKS),
+        ("done", ctypes.c_void_p),
+    ]
 
 _lib: ctypes.CDLL | None = None
 
@@ -361,3 +387,73 @@ def paged_decode_cascade(
         "kl_paged_decode_cascade",
     )
     return scratch
+
+
+def paged_decode_gather(
+    gather: HeadGather,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    scratch: DecodeScratch | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> DecodeScratch:
+    """kl_paged_decode_gather: this rank's KV-head shard, its heads stored into every rank's output."""
+    batch, hq, d = q.shape
+    num_pages, page, hkv, _ = k_cache.shape
+    if scratch is None:
+        scratch = DecodeScratch.for_problem(q, k_cache, block_table)
+    scale = d**-0.5 if scale is None else scale
+    _check(
+        load().kl_paged_decode_gather(
+            DTYPE_CODES[q.dtype], ctypes.byref(gather), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(block_table),
+            _ptr(seq_lens), batch, hq, hkv, d, page, block_table.stride(0), block_table.shape[1], num_pages, scale,
+            _ptr(scratch.partials), scratch.partials.numel(), _ptr(scratch.sync), scratch.sync.numel(),
+            _stream(stream),
+        ),
+        "kl_paged_decode_gather",
+    )
+    return scratch
+
+
+def ipc_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Zeroed device memory on the current device that peers can map: (pointer, handle bytes)."""
+    ptr = ctypes.c_void_p(0)
+    handle = ctypes.create_string_buffer(KL_IPC_HANDLE_BYTES)
+    _check(load().kl_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "kl_ipc_alloc")
+    return int(ptr.value), handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer's kl_ipc_alloc buffer into this process (current device); returns its address here."""
+    if len(handle) != KL_IPC_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {KL_IPC_HANDLE_BYTES} bytes, not {len(handle)}")
+    ptr = ctypes.c_void_p(0)
+    buf = ctypes.create_string_buffer(handle, KL_IPC_HANDLE_BYTES)
+    _check(load().kl_ipc_open(buf, ctypes.byref(ptr)), "kl_ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(load().kl_ipc_close(ptr), "kl_ipc_close")
+
+
+def ipc_free(ptr: int) -> None:
+    _check(load().kl_ipc_free(ptr), "kl_ipc_free")
+
+
+class _DeviceArray:
+    """A raw device buffer described by the CUDA array interface (torch.as_tensor wraps it without a copy)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 2,
+                                         "strides": None}
+
+
+def device_tensor(ptr: int, shape: tuple[int, ...], dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A tensor view of `shape` over device memory at `ptr` (not owned: the memory must outlive it)."""
+    typestr = {torch.float32: "<f4", torch.float16: "<f2", torch.bfloat16: "<i2"}[dtype]
+    t = torch.as_tensor(_DeviceArray(ptr, tuple(shape), typestr), device=device)
+    return t.view(dtype) if dtype == torch.bfloat16 else t

@@ -44,6 +44,15 @@ class PagedKV:
         return self.k_cache.shape[0]
 
 
+def config4_lengths(batch: int = 128, seed: int = 4) -> list[int]:
+    """Config 4's ragged batch: lengths uniform in [1, 32768] from a seeded generator, the first
+    three replaced by 16k - 1, 16k and 16k + 1 (at and around a multiple of the page size)."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    return [16383, 16384, 16385] + rng.integers(1, 32769, size=batch - 3).tolist()
+
+
 def pages_for(seq_len: int, page_size: int) -> int:
     return (seq_len + page_size - 1) // page_size
 

@@ -98,9 +98,8 @@ def paged_decode_attention(
     length 0 yields zeros, as the reference's empty einsum does.
     """
     q = np.asarray(q, dtype=np.float32)
-    batch, num_q_heads, head_dim = q.shape
-    _, page_size, num_kv_heads, _ = k_cache.shape
-    group = num_q_heads // num_kv_heads
+    batch, _, head_dim = q.shape
+    page_size = k_cache.shape[1]
     scale = head_dim**-0.5 if scale is None else scale
     out = np.zeros_like(q)
     for b in range(batch):
@@ -108,18 +107,34 @@ def paged_decode_attention(
         if length == 0:
             continue
         pages = np.asarray(block_table[b, : (length + page_size - 1) // page_size], dtype=np.int64)
-        k = np.asarray(k_cache[pages], np.float32).reshape(-1, num_kv_heads, head_dim)[:length]
-        v = np.asarray(v_cache[pages], np.float32).reshape(-1, num_kv_heads, head_dim)[:length]
-        # [L, Hkv, D] -> [Hkv, L, D]; query heads grouped per KV head: [Hkv, G, D].
-        k = np.ascontiguousarray(k.transpose(1, 0, 2))
-        v = np.ascontiguousarray(v.transpose(1, 0, 2))
-        qb = q[b].reshape(num_kv_heads, group, head_dim)
-        scores = np.matmul(qb, k.transpose(0, 2, 1)) * np.float32(scale)  # [Hkv, G, L]
-        scores -= scores.max(axis=-1, keepdims=True)
-        probs = np.exp(scores, dtype=np.float32)
-        probs /= probs.sum(axis=-1, keepdims=True, dtype=np.float32)
-        out[b] = np.matmul(probs, v).reshape(num_q_heads, head_dim)
+        k = _token_rows(k_cache, pages, length)  # [L, Hkv, D]
+        v = _token_rows(v_cache, pages, length)
+        out[b] = _attend(q[b], k, v, scale)
     return round_to(out, dtype)
+
+
+def _attend(qb: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:
+    """softmax(scale * q . K^T) V for one sequence, fp32 (kernel_lab/reference.py:62-67): qb [Hq, D],
+    k and v [L, Hkv, D], query head h attending with KV head h // (Hq / Hkv)."""
+    num_q_heads, head_dim = qb.shape
+    num_kv_heads = k.shape[1]
+    q3 = qb.reshape(num_kv_heads, num_q_heads // num_kv_heads, head_dim)
+    scores = np.einsum("hgd,lhd->hgl", q3, k, optimize=True) * np.float32(scale)  # [Hkv, G, L]
+    scores -= scores.max(axis=-1, keepdims=True)
+    probs = np.exp(scores, dtype=np.float32)
+    probs /= probs.sum(axis=-1, keepdims=True, dtype=np.float32)
+    return np.einsum("hgl,lhd->hgd", probs, v, optimize=True).reshape(num_q_heads, head_dim)
+
+
+def _token_rows(cache: np.ndarray, pages: np.ndarray, length: int) -> np.ndarray:
+    """The first `length` token rows [L, Hkv, D] (fp32) of the pages `pages` of a paged cache: a
+    view when the pages are consecutive, else a gather."""
+    _, page_size, num_kv_heads, head_dim = cache.shape
+    if len(pages) and pages[0] >= 0 and np.array_equal(pages, np.arange(pages[0], pages[0] + len(pages))):
+        rows = cache[pages[0] : pages[0] + len(pages)]
+    else:
+        rows = cache[pages]
+    return np.asarray(rows, np.float32).reshape(-1, num_kv_heads, head_dim)[:length]
 
 
 def _gather_tokens(cache: np.ndarray, pages_row: np.ndarray, length: int) -> np.ndarray:
@@ -150,9 +165,7 @@ def paged_decode_attention_cascade(
     last entry batch) makes the prefixes ignored, as the kernel does.
     """
     q = np.asarray(q, dtype=np.float32)
-    batch, num_q_heads, head_dim = q.shape
-    num_kv_heads = k_cache.shape[2]
-    group = num_q_heads // num_kv_heads
+    batch, _, head_dim = q.shape
     scale = head_dim**-0.5 if scale is None else scale
     indptr = np.asarray(prefix_indptr, dtype=np.int64)
     groups = len(prefix_lens)
@@ -174,14 +187,7 @@ def paged_decode_attention_cascade(
             vs.append(_gather_tokens(v_cache, block_table[b], length))
         if not ks:
             continue
-        k = np.ascontiguousarray(np.concatenate(ks).transpose(1, 0, 2))
-        v = np.ascontiguousarray(np.concatenate(vs).transpose(1, 0, 2))
-        qb = q[b].reshape(num_kv_heads, group, head_dim)
-        scores = np.matmul(qb, k.transpose(0, 2, 1)) * np.float32(scale)
-        scores -= scores.max(axis=-1, keepdims=True)
-        probs = np.exp(scores, dtype=np.float32)
-        probs /= probs.sum(axis=-1, keepdims=True, dtype=np.float32)
-        out[b] = np.matmul(probs, v).reshape(num_q_heads, head_dim)
+        out[b] = _attend(q[b], np.concatenate(ks), np.concatenate(vs), scale)
     return round_to(out, dtype)
 
 

@@ -36,6 +36,11 @@ def test_header_declares_the_abi():
         "kl_paged_decode",
         "kl_paged_decode_attention",
         "kl_paged_decode_read_status",
+        "kl_paged_decode_gather",
+        "kl_ipc_alloc",
+        "kl_ipc_open",
+        "kl_ipc_close",
+        "kl_ipc_free",
         "kl_paged_decode_noalloc",
         "kl_paged_decode_noalloc_read_status",
         "kl_paged_kv_append",
@@ -101,6 +106,25 @@ def test_noop_and_validation_without_a_device():
     assert cas(2, 4, 2, 1, pstride=3) == CUDA_ERROR_INVALID_VALUE
     assert lib.kl_paged_decode_cascade_workspace_size(2, 0, 1, 32, 8, 128, 16, 4, 4, ctypes.byref(size),
                                                       ctypes.byref(size)) == 0
+    # Fused head gather: a rank outside the group, a missing peer output or flags, or a first epoch
+    # of 0 is rejected before any launch; batch 0 with a valid descriptor is a no-op.
+    g = capi.HeadGather()
+    g.num_ranks, g.rank, g.epoch, g.done = 2, 0, 1, 1
+    g.out[0], g.out[1], g.flags[0], g.flags[1] = 1, 1, 1, 1
+    gat = lambda desc, batch: lib.kl_paged_decode_gather(  # noqa: E731
+        2, ctypes.byref(desc), *([1] * 5), batch, 16, 4, 128, 16, 4, 4, 10, 0.1, 1, 1 << 20, 1, 1 << 20, None)
+    assert gat(g, 0) == 0
+    g.rank = 2
+    assert gat(g, 4) == CUDA_ERROR_INVALID_VALUE
+    g.rank, g.flags[1] = 0, None
+    assert gat(g, 4) == CUDA_ERROR_INVALID_VALUE
+    g.flags[1], g.epoch = 1, 0
+    assert gat(g, 4) == CUDA_ERROR_INVALID_VALUE
+    assert lib.kl_paged_decode_gather(2, None, *([1] * 5), 4, 16, 4, 128, 16, 4, 4, 10, 0.1, 1, 1, 1, 1, None) == (
+        CUDA_ERROR_INVALID_VALUE
+    )
+    assert lib.kl_ipc_open(None, None) == CUDA_ERROR_INVALID_VALUE
+    assert lib.kl_ipc_close(None) == 0 and lib.kl_ipc_free(None) == 0
 
 
 # kernel-lab's schema strings, verbatim (csrc/torch_bindings.cpp:108-113 there).

@@ -131,3 +131,47 @@ def test_head_ranges_and_shards_cover_the_problem():
     np.testing.assert_array_equal(torch.cat([p[1] for p in parts], dim=2).numpy(), kv.k_cache.numpy())
     # world size 1: the gather is the identity.
     assert gather_heads(q, 1) is q
+
+
+def _exchange_worker(rank, world, port, result_q):
+    _paths()
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        from kernel_lab.sharding import exchange, require_distinct_devices
+
+        # Handles of the fused head gather's buffers (64 bytes each) reach every rank in rank order.
+        handles = exchange(bytes([rank]) * 64)
+        # Two ranks that report one GPU are refused before any kernel could wait on the other.
+        refused = False
+        try:
+            require_distinct_devices(exchange("same-gpu"))
+        except RuntimeError:
+            refused = True
+        require_distinct_devices(exchange(f"gpu-{rank}"))
+        dist.destroy_process_group()
+        result_q.put((rank, handles == [bytes([r]) * 64 for r in range(world)], refused, None))
+    except Exception:
+        result_q.put((rank, False, False, traceback.format_exc()))
+
+
+def test_fused_gather_host_logic_on_gloo_ranks():
+    """The host side of PeerHeadGather across two CPU ranks: IPC handles exchanged in rank order,
+    ranks on one device refused, and the call numbers (epochs) that key the output regions."""
+    _paths()
+    from kernel_lab.sharding import next_epoch
+
+    assert next_epoch(0) == 1 and next_epoch(7) == 8
+    assert next_epoch((1 << 32) - 1) == 1  # 0 is never a call number
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ordered, refused, err in results:
+        assert err is None, f"rank {rank}: {err}"
+        assert ordered and refused

@@ -1,4 +1,7 @@
-"""KV-head-sharded decode on real GPUs: one process per GPU, NCCL all-gather (config 5's layout).
+"""KV-head-sharded decode on real GPUs: one process per GPU (config 5's layout).
+
+Two gathers of the heads are tested: the product path, where the decode kernel stores its rows
+into every rank's output over NVLink (``PeerHeadGather``), and the NCCL all-gather baseline.
 
 Needs at least two visible GPUs; skipped otherwise. Each rank runs the single-GPU CUDA op on its
 own KV heads; each rank's slice of the gathered output must equal its own local output bit for
@@ -93,4 +96,68 @@ def test_sharded_decode_on_two_gpus_matches_the_unsharded_op():
     for rank, same, status, err in results:
         assert err is None, f"rank {rank}: {err}"
         assert same, f"rank {rank}: sharded output differs from the unsharded op"
+        assert status == 0
+
+
+def _peer_worker(rank, world, port, result_q):
+    _paths()
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        from kernel_lab import cuda_ops
+        from kernel_lab.sharding import PeerHeadGather, gather_heads, shard_heads
+
+        errors = []
+        q, kv = _problem(dev)
+        q_l, k_l, v_l = shard_heads(q, kv.k_cache, kv.v_cache, world, rank)
+        want = cuda_ops.paged_decode_attention(q, kv.k_cache, kv.v_cache, kv.block_table, kv.seq_lens, 128**-0.5)
+        local = cuda_ops.paged_decode_attention(q_l, k_l, v_l, kv.block_table, kv.seq_lens, 128**-0.5)
+        nccl = gather_heads(local, world)
+        gather = PeerHeadGather(q.shape[0], q_l.shape[1], 128, torch.bfloat16)
+        hq_l = q_l.shape[1]
+        # Five calls in a row (regions rotate), each checked before the next one is enqueued; the
+        # third call gets a different q (scaled), so stale rows from an earlier call would show.
+        for call in range(5):
+            qc = q_l * 0.5 if call == 2 else q_l
+            got = gather(qc, k_l, v_l, kv.block_table, kv.seq_lens, 128**-0.5)
+            torch.cuda.synchronize()
+            if call == 2:
+                ref_local = cuda_ops.paged_decode_attention(qc, k_l, v_l, kv.block_table, kv.seq_lens, 128**-0.5)
+                if not torch.equal(got[:, rank * hq_l : (rank + 1) * hq_l], ref_local):
+                    errors.append(f"call {call}: own heads differ from the local op")
+                continue
+            if not torch.equal(got[:, rank * hq_l : (rank + 1) * hq_l], local):
+                errors.append(f"call {call}: own heads differ from the local op")
+            if not torch.equal(got, nccl):
+                errors.append(f"call {call}: differs from the NCCL all-gather of the same shards")
+            if not torch.allclose(got.float(), want.float(), atol=1.6e-2, rtol=1.6e-2):
+                errors.append(f"call {call}: not close to the unsharded op")
+        status = gather.status(clear=True)
+        gather.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        result_q.put((rank, not errors, status, "; ".join(errors) or None))
+    except Exception:
+        result_q.put((rank, False, -1, traceback.format_exc()))
+
+
+def test_fused_peer_gather_on_two_gpus_matches_nccl_and_the_unsharded_op():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, status, err in results:
+        assert err is None, f"rank {rank}: {err}"
+        assert ok
         assert status == 0
