@@ -131,7 +131,12 @@ def workload_spec(name: str, world: int) -> dict:
 
 
 class ClockSampler:
-    """Polls NVML (SM clock, clock-event reasons) every few ms on a side thread."""
+    """Polls NVML (SM clock, clock-event reasons) on a side thread, every `period` seconds.
+
+    Each poll briefly stalls the polled GPU; a multi-GPU step waits for its slowest rank, so with
+    every rank polling the stalls added up with N (measured at N = 8: 279 us per step polled every
+    5 ms on every rank against 210 us without polling). Multi-GPU runs therefore poll rank 0's GPU
+    only, every 20 ms (`enabled` False on the other ranks)."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -139,10 +144,14 @@ class ClockSampler:
         "display_clock_setting": 0x100,
     }
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period: float = 0.005, enabled: bool = True):
         self.samples: list[tuple[int, int]] = []
         self.max_mhz = None
+        self.period = period
         self._stop = threading.Event()
+        self._nvml = None
+        if not enabled:
+            return
         try:
             import pynvml
 
@@ -165,7 +174,7 @@ class ClockSampler:
                 self._sample()
             except Exception:
                 return
-            time.sleep(0.005)
+            time.sleep(self.period)
 
     def __enter__(self):
         if self._nvml:
@@ -666,7 +675,8 @@ def main() -> None:
         # kernels excepted), so the region's two events give the kernel's average launch duration
         # (an event between back-to-back launches would add ~5 us of launch gap to every step).
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(torch.cuda.current_device()) as clocks:
+        with ClockSampler(torch.cuda.current_device(), period=0.005 if world == 1 else 0.02,
+                          enabled=rank == 0) as clocks:
             torch.cuda.synchronize()
             t0.record(stream)
             for i in range(steps):
@@ -727,6 +737,23 @@ def main() -> None:
             status = gather.status(clear=True) if gather is not None else cuda_ops.decode_status(clear=True)
         else:
             status = 0
+        if gather is not None and not args.no_extras:
+            # Where the step's time goes at N > 1: the same shard through the plain op (no gather),
+            # and the gathered step timed again without the clock sampler; max over ranks.
+            def plain(i=0):
+                torch.ops.kernel_lab.paged_decode_attention(out_local, q, kv.k_cache, kv.v_cache, kv.block_table,
+                                                            kv.seq_lens, scale)
+
+            for _ in range(3):
+                plain()
+            diag = torch.tensor([time_back_to_back(plain, steps, stream), 0.0], device=dev, dtype=torch.float64)
+            dist.barrier()
+            diag[1] = time_back_to_back(step, steps, stream)
+            dist.all_reduce(diag, op=dist.ReduceOp.MAX)
+            extra["diagnostics"] = {"shard_plain_op_us": round(diag[0].item() * 1e3, 2),
+                                    "gathered_step_no_sampler_us": round(diag[1].item() * 1e3, 2),
+                                    "note": "max over ranks; the shard's own kernel without the gather, and the "
+                                            "timed step repeated without the NVML clock sampler"}
         if spec["kind"] == "decode" and args.workload == "decode" and world == 1 and not args.no_extras:
             extra["grid"] = decode_grid(dev, stream, min(steps, 100), peaks.hbm_gbps)
             extra["secondary"] = rmsnorm_secondary(dev, stream, steps, peaks.hbm_gbps)

@@ -6,10 +6,11 @@ for sm_100a, into oracle/_ref/libkernel_lab_ref.so. Nothing is copied from the r
 its own build system (setup.py / torch extension) is not used: the two kernel files and their
 header need nothing but the CUDA toolkit (kernel-lab csrc/kernel_lab.h:1-3).
 
-Only tests/ load the result. When the reference tree is absent (the GPU box), nothing is built
-and the prebuilt library, if any, is used as is.
+Only tests/ load the result. The reference tree is given by --reference or the environment
+variable KL_REFERENCE_DIR; without one (the GPU box has no reference tree), nothing is built and
+the prebuilt library, if any, is used as is.
 
-    python oracle/build_ref.py [--reference DIR]
+    python oracle/build_ref.py --reference DIR
 """
 
 from __future__ import annotations
@@ -22,12 +23,19 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 LIB = OUT_DIR / "libkernel_lab_ref.so"
-DEFAULT_REFERENCE = Path(os.environ.get("KL_REFERENCE_DIR", "/root/reference"))
 SOURCES = ("csrc/paged_attention.cu", "csrc/rmsnorm.cu")
 
 
-def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path | None:
+def reference_from_env() -> Path | None:
+    env = os.environ.get("KL_REFERENCE_DIR")
+    return Path(env) if env else None
+
+
+def build(reference: Path | None = None, force: bool = False) -> Path | None:
     """Compile the comparator library; returns its path, or None without the reference tree."""
+    reference = reference if reference is not None else reference_from_env()
+    if reference is None:
+        return LIB if LIB.exists() else None
     srcs = [reference / s for s in SOURCES]
     if not all(s.exists() for s in srcs):
         return LIB if LIB.exists() else None
@@ -45,7 +53,8 @@ def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path | No
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", type=Path, default=reference_from_env(),
+                    help="kernel-lab's source tree (default: $KL_REFERENCE_DIR)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     print(build(a.reference, a.force))

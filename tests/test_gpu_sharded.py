@@ -43,12 +43,12 @@ def _paths():
             sys.path.insert(0, p)
 
 
-def _problem(device):
+def _problem(device, hq=64, hkv=8):
     from kernel_lab.kv_cache import random_paged_pool
 
     # Config 5's heads (64 query / 8 KV, D 128, bf16) on ragged lengths across page boundaries.
     lens = [1, 15, 16, 17, 300, 1025, 4096, 777]
-    return random_paged_pool(lens, 64, 8, 128, 16, dtype=torch.bfloat16, device=device, seed=21)
+    return random_paged_pool(lens, hq, hkv, 128, 16, dtype=torch.bfloat16, device=device, seed=21)
 
 
 def _worker(rank, world, port, result_q):
@@ -99,7 +99,7 @@ def test_sharded_decode_on_two_gpus_matches_the_unsharded_op():
         assert status == 0
 
 
-def _peer_worker(rank, world, port, result_q):
+def _peer_worker(rank, world, port, result_q, hq=64, hkv=8):
     _paths()
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -112,7 +112,7 @@ def _peer_worker(rank, world, port, result_q):
         from kernel_lab.sharding import PeerHeadGather, gather_heads, shard_heads
 
         errors = []
-        q, kv = _problem(dev)
+        q, kv = _problem(dev, hq, hkv)
         q_l, k_l, v_l = shard_heads(q, kv.k_cache, kv.v_cache, world, rank)
         want = cuda_ops.paged_decode_attention(q, kv.k_cache, kv.v_cache, kv.block_table, kv.seq_lens, 128**-0.5)
         local = cuda_ops.paged_decode_attention(q_l, k_l, v_l, kv.block_table, kv.seq_lens, 128**-0.5)
@@ -145,13 +145,16 @@ def _peer_worker(rank, world, port, result_q):
         result_q.put((rank, False, -1, traceback.format_exc()))
 
 
-def test_fused_peer_gather_on_two_gpus_matches_nccl_and_the_unsharded_op():
+@pytest.mark.parametrize("hq,hkv", [(64, 8), (8, 2)], ids=["4_kv_heads_a_rank", "1_kv_head_a_rank"])
+def test_fused_peer_gather_on_two_gpus_matches_nccl_and_the_unsharded_op(hq, hkv):
+    """With one KV head a rank (as Llama-3 heads sharded 8 ways) each warp of the kernel walks its
+    own stream of the plan; with four, the warps of a tile share one ring."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q, hq, hkv)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
