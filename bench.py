@@ -72,6 +72,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-extras", action="store_true", help="skip the grid and secondary objects of the default line")
     ap.add_argument("--batch", type=int, help="override the workload's batch (per GPU for weak scaling)")
     ap.add_argument("--ctx", type=int, help="override the workload's context length")
+    ap.add_argument("--heads", help="override the decode workload's heads as HQ/HKV (e.g. 4/1: one GPU's share "
+                                    "of Llama-3-8B's heads sharded 8 ways)")
     return ap.parse_args()
 
 
@@ -475,6 +477,11 @@ def main() -> None:
     if args.ctx and spec["kind"] == "decode":
         spec["ctx"] = args.ctx
         spec["desc"] += f" (ctx overridden: {args.ctx})"
+    if args.heads and spec["kind"] == "decode":
+        if world > 1 and spec["layout"] == "kv_heads":
+            raise SystemExit("--heads sets one GPU's heads; the KV-head split at N>1 derives them")
+        spec["hq"], spec["hkv"] = (int(x) for x in args.heads.split("/"))
+        spec["desc"] += f" (heads overridden: {args.heads})"
     if args.batch and spec["kind"] == "rmsnorm":
         spec["rows"] = args.batch
         spec["desc"] += f" (rows overridden: {args.batch})"
@@ -783,7 +790,7 @@ def main() -> None:
                                  "NVLink (CUDA IPC peer stores, no multicast), one launch per step")
         elif spec["kind"] == "ragged":
             cfg.update(batch=spec["batch"], head_dim=128, page_size=16, lengths="U[1, 32768] seed 4 + 16383/16384/16385",
-                       layouts={k: f"{v['hq']}/{v['hkv']}" for k, v in RAGGED_LAYOUTS.items()})
+                       layouts={k: f"{hq}/{hkv}" for k, (hq, hkv) in RAGGED_LAYOUTS.items()})
         else:
             cfg.update(rows=spec["rows"], hidden=spec["hidden"], eps=1e-5)
         if "grid" in extra:

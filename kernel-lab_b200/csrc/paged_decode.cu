@@ -925,7 +925,10 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int HT = cfg.ht, HG = cfg.hg, TW = cfg.tw, nstage = cfg.nstage;
-  const TcLayout L = tc_layout(D, NT, TW, cfg.ns, nstage, a.batch, EB, a.num_prefixes, HT);
+  // Streams exist only in the one-n-tile kernels; the others see the constant 1 (a runtime value
+  // there raised the two-n-tile kernel's spills from 1,364 to 2,024 bytes).
+  const int NS = NT == 1 ? cfg.ns : 1;  // streams (ranges) of this CTA
+  const TcLayout L = tc_layout(D, NT, TW, NS, nstage, a.batch, EB, a.num_prefixes, HT);
   const uint32_t ring = smem_u32(smem + L.ring);
   const uint32_t bars = smem_u32(smem + L.bars);
   float* red_m = reinterpret_cast<float*>(smem + L.red_m);
@@ -954,8 +957,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   // combine at the end of a segment. Streams measured 205.5 -> 186.2 us at 512 sequences x 4096
   // tokens of one KV head (Llama-3-8B heads sharded 8 ways), and slower than the shared ring with
   // two or four warps a stream (their ranges cut the plan 2-4 times finer: more split merges).
-  const int NS = NT == 1 ? cfg.ns : 1;  // streams (ranges) of this CTA
-  const int SPS = nstage / NS;             // stages per stream (nstage is a multiple of TW)
+  const int SPS = nstage / NS;  // stages per stream (nstage is a multiple of TW)
   if (threadIdx.x == 0) {
     for (int s = 0; s < nstage; ++s) {
       mbar_init(bars + 8u * s, 1);                   // full: the producer's expect_tx arrival
