@@ -135,16 +135,37 @@ def workload_spec(name: str, world: int) -> dict:
 class ClockSampler:
     """Polls NVML (SM clock, clock-event reasons) on a side thread, every `period` seconds.
 
-    Each poll briefly stalls the polled GPU; a multi-GPU step waits for its slowest rank, so with
-    every rank polling the stalls added up with N (measured at N = 8: 279 us per step polled every
-    5 ms on every rank against 210 us without polling). Multi-GPU runs therefore poll rank 0's GPU
-    only, every 20 ms (`enabled` False on the other ranks)."""
+    NVML is initialised once per process by `ClockSampler.init`, before the problem is built and
+    warmed up: initialising it enumerates every GPU of the node, and done at the start of a timed
+    region it stalled the multi-GPU step for milliseconds (8 GPUs: 251 us per step against 209 us;
+    an `nvidia-smi` process polling alongside slowed the 2-GPU step tenfold). Polls of an
+    initialised handle measured free (2 GPUs: 176.6-176.9 us per step polled every 20 ms against
+    175.4-178.8 us unpolled). Multi-GPU runs poll rank 0's GPU only, every 20 ms (`enabled` False
+    on the other ranks): a step waits for its slowest rank."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
         "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
         "display_clock_setting": 0x100,
     }
+    _nvml = None
+    _handles: dict = {}
+
+    @classmethod
+    def init(cls, device_index: int) -> None:
+        """Initialises NVML and this GPU's handle (once; no clocks are reported if NVML is absent)."""
+        if device_index in cls._handles:
+            return
+        try:
+            import pynvml
+
+            if cls._nvml is None:
+                pynvml.nvmlInit()
+                cls._nvml = pynvml
+            h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            cls._handles[device_index] = (h, pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            pass
 
     def __init__(self, device_index: int, period: float = 0.005, enabled: bool = True):
         self.samples: list[tuple[int, int]] = []
@@ -152,17 +173,10 @@ class ClockSampler:
         self.period = period
         self._stop = threading.Event()
         self._nvml = None
-        if not enabled:
+        if not enabled or device_index not in ClockSampler._handles:
             return
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self._nvml = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-        except Exception:  # no NVML: report no clocks
-            self._nvml = None
+        self._nvml = ClockSampler._nvml
+        self._h, self.max_mhz = ClockSampler._handles[device_index]
 
     def _sample(self):
         n = self._nvml
@@ -508,6 +522,8 @@ def main() -> None:
         raise SystemExit(f"kernel_lab CUDA path unavailable: {cuda_ops.why_unavailable()}")
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream()
+    if world == 1 or rank == 0:
+        ClockSampler.init(torch.cuda.current_device())
     peaks = measured_peaks()
     steps = args.steps
     warmup = max(args.warmup, 3)
@@ -641,7 +657,8 @@ def main() -> None:
             step_ms += ms
             gbs = lay["work"].bytes / (ms * 1e-3) / 1e9
             lay.update(us=round(ms * 1e3, 2), gbs=round(gbs, 1), frac=round(gbs / peaks.hbm_gbps, 4),
-                       kv_bytes=int(lay["work"].bytes), status=cuda_ops.decode_status(clear=True))
+                       algorithmic_bytes=int(lay["work"].bytes), traffic=load_traffic(f"decode_ragged_{name}_n1"),
+                       status=cuda_ops.decode_status(clear=True))
 
             def dec(q_t, bt_t, ln_t, out_t, kv=kv):
                 torch.ops.kernel_lab.paged_decode_attention(out_t, q_t, kv.k_cache, kv.v_cache, bt_t, ln_t, 128**-0.5)
@@ -772,6 +789,9 @@ def main() -> None:
         achieved = kernel_work.bytes / (kern_ms * 1e-3) / 1e9
         key = f"{args.workload}_n{world}"
         traffic = load_traffic(key)
+        if spec["kind"] == "ragged":  # one launch of each layout per step
+            per_layout = [v.get("traffic") for v in extra["layouts"].values()]
+            traffic = sum(per_layout) if all(t is not None for t in per_layout) else None
         value = job_bytes / (step_ms * 1e-3) / 1e9
         cpu = None
         # kernel-lab has no e4m3 or cascade path to time on the host
@@ -784,7 +804,7 @@ def main() -> None:
         if spec["kind"] == "decode":
             cfg.update(batch=spec["batch"], ctx=spec["ctx"], num_q_heads=spec["hq"], num_kv_heads=spec["hkv"],
                        head_dim=spec["d"], page_size=spec["page"], pool_pages=int(kv.k_cache.shape[0]),
-                       kv_bytes_per_gpu=int(kernel_work.bytes), planner="load-balanced (num_splits=0)")
+                       algorithmic_bytes_per_gpu=int(kernel_work.bytes), planner="load-balanced (num_splits=0)")
             if gather is not None:
                 cfg["gather"] = ("fused: the decode kernel stores every rank's heads into every rank's output over "
                                  "NVLink (CUDA IPC peer stores, no multicast), one launch per step")

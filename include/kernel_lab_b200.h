@@ -41,7 +41,7 @@ enum {
   KL_STATUS_LEN_CLAMPED = 2,  /* a sequence longer than max_pages_per_seq * page_size was clamped */
   KL_STATUS_WAIT_TIMEOUT = 4,  /* an internal pipeline wait exceeded its time limit; output is invalid */
   KL_STATUS_BAD_PREFIX_GROUPS = 8, /* cascade: prefix_indptr is not a partition of the batch; prefixes ignored */
-  KL_STATUS_PEER_TIMEOUT = 16      /* head gather: another rank's arrival did not come within 10 s */
+  KL_STATUS_PEER_TIMEOUT = 16      /* head gather: another rank's arrival did not come in time */
 };
 
 /* Library version string, e.g. "kernel_lab_b200 0.1.0 sm_100a". */
@@ -135,8 +135,8 @@ int kl_paged_decode_read_status(void* sync, uint32_t* status, int clear, void* s
  * arrived at call e. Alternate the output regions by epoch: two regions when every reader of a
  * call's output is stream-ordered before the rank's next call, three when a reader (a copy on
  * another stream, say) only has to finish before the call after next. A rank whose peers do not
- * arrive within 10 s sets KL_STATUS_PEER_TIMEOUT in `sync` and returns (its output is then
- * incomplete).
+ * arrive within timeout_ms (0: 10 s) sets KL_STATUS_PEER_TIMEOUT in `sync` and returns (its
+ * output then lacks the late ranks' heads; its own heads are stored).
  * num_ranks == 1: plain kl_paged_decode into out[0].
  *
  * Tensor-core shapes only (fp16/bf16, head_dim 64/128/256, page size 8 or a multiple of 16, the
@@ -153,6 +153,7 @@ typedef struct kl_head_gather {
   void* out[KL_GATHER_MAX_RANKS];
   uint32_t* flags[KL_GATHER_MAX_RANKS];
   uint32_t* done;
+  uint32_t timeout_ms; /* wait for the peers' arrivals; 0: 10 s */
 } kl_head_gather_t;
 
 int kl_paged_decode_gather(int dtype, const kl_head_gather_t* gather, const void* q, const void* k_cache,

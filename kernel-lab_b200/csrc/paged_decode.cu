@@ -73,7 +73,7 @@ constexpr int kMaxBatch = 16384;  // the plan lives in shared memory
 constexpr int kMaxHeadGroups = 4; // query-head groups per KV head (counter stride)
 constexpr uint64_t kWaitLimit = 2000000000ull;  // SM cycles: about one second at 1.9 GHz
 constexpr int kMaxRanks = KL_GATHER_MAX_RANKS;   // GPUs of one head gather
-constexpr uint64_t kPeerWaitNs = 10000000000ull; // a rank waits this long (10 s) for its peers' arrivals
+constexpr uint64_t kPeerWaitNs = 10000000000ull; // default wait (10 s) of a rank for its peers' arrivals
 
 // Head gather over NVLink (ranks > 1): every final output row is stored to this rank's output
 // and, with plain peer stores, to the same place in every other rank's (out[r]: rank r's output
@@ -87,6 +87,7 @@ struct Gather {
   void* out[kMaxRanks];
   uint32_t* flags[kMaxRanks];  // rank r's arrival flags [ranks]
   uint32_t* done;              // this rank's count of finished CTAs (zero at rest)
+  uint64_t wait_ns;            // how long the last CTA waits for the peers' arrivals
 };
 
 struct DecodeArgs {
@@ -787,7 +788,7 @@ __device__ __forceinline__ void cascade_arrive(const DecodeArgs& a, const RowSin
 // releases: a peer that acquires its flag sees every row this GPU stored (release and acquire are
 // cumulative along the chain barrier, GPU-scope count, system-scope flag). It then waits until
 // every rank's epoch has arrived in this rank's flags (an epoch at or past this launch's also
-// counts: a peer may already be one launch ahead), for at most kPeerWaitNs; on timeout it sets
+// counts: a peer may already be one launch ahead), for at most g.wait_ns; on timeout it sets
 // kStatusPeerTimeout and leaves. It returns the count to zero for the next launch. One system-scope
 // fence per launch instead of one per thread: measured 176 against 188 us at two GPUs.
 __device__ void gather_finish(const DecodeArgs& a, int nthreads) {
@@ -802,7 +803,7 @@ __device__ void gather_finish(const DecodeArgs& a, int nthreads) {
   bool late = false;
   for (int r = 0; r < g.ranks && !late; ++r) {
     while (static_cast<int32_t>(ld_acquire_sys(own + r) - g.epoch) < 0) {
-      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+      if (globaltimer_ns() - t0 > g.wait_ns) {
         atomicOr(a.sync, kStatusPeerTimeout);
         late = true;
         break;
@@ -2848,6 +2849,7 @@ int decode_impl(int dtype, void* out, const void* q, const void* k_cache, const 
       a.gat.rank = gather->rank;
       a.gat.epoch = gather->epoch;
       a.gat.done = gather->done;
+      a.gat.wait_ns = gather->timeout_ms ? gather->timeout_ms * 1000000ull : kPeerWaitNs;
       for (int r = 0; r < gather->num_ranks; ++r) {
         a.gat.out[r] = static_cast<uint8_t*>(gather->out[r]) + head_off;
         a.gat.flags[r] = gather->flags[r];

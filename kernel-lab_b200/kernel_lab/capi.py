@@ -100,6 +100,7 @@ class HeadGather(ctypes.Structure):
         ("out", ctypes.c_void_p * KL_GATHER_MAX_RANKS),
         ("flags", ctypes.c_void_p * KL_GATHER_MAX_RANKS),
         ("done", ctypes.c_void_p),
+        ("timeout_ms", ctypes.c_uint32),
     ]
 
 _lib: ctypes.CDLL | None = None

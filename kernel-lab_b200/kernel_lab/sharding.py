@@ -142,10 +142,12 @@ class PeerHeadGather:
     number: the output of a call stays valid until the call two after it runs on this rank's
     stream (a peer may be one call ahead). Every rank must make the same calls in the same
     order, on distinct GPUs. With one rank it is the plain decode into a local region.
+    A rank whose peers do not arrive within ``timeout_ms`` (0: 10 s) returns with
+    ``KL_STATUS_PEER_TIMEOUT`` in ``status()``.
     """
 
     def __init__(self, batch: int, num_q_heads: int, head_dim: int, dtype: torch.dtype = torch.bfloat16,
-                 group=None, slots: int = 3):
+                 group=None, slots: int = 3, timeout_ms: int = 0):
         from kernel_lab import capi
 
         if slots < 2:
@@ -185,6 +187,7 @@ class PeerHeadGather:
         for r in range(self.world):
             g.flags[r] = bases[r] + flags_off
         g.done = bases[self.rank] + done_off
+        g.timeout_ms = timeout_ms
         self._g = g
         self.epoch = 0
         self.scratch = None
