@@ -138,10 +138,12 @@ class ClockSampler:
     NVML is initialised once per process by `ClockSampler.init`, before the problem is built and
     warmed up: initialising it enumerates every GPU of the node, and done at the start of a timed
     region it stalled the multi-GPU step for milliseconds (8 GPUs: 251 us per step against 209 us;
-    an `nvidia-smi` process polling alongside slowed the 2-GPU step tenfold). Polls of an
-    initialised handle measured free (2 GPUs: 176.6-176.9 us per step polled every 20 ms against
-    175.4-178.8 us unpolled). Multi-GPU runs poll rank 0's GPU only, every 20 ms (`enabled` False
-    on the other ranks): a step waits for its slowest rank."""
+    an `nvidia-smi` process polling alongside slowed the 2-GPU step tenfold). One poll is taken
+    before the region; the side thread starts polling only once the host has enqueued every timed
+    step (`launched`), so the polls fall while the GPU works through the region and never meet
+    the launch burst. Polls taken that way measured free (2 GPUs: 176.6-176.9 us per step polled
+    every 20 ms against 175.4-178.8 us unpolled). Multi-GPU runs poll rank 0's GPU only, every
+    20 ms (`enabled` False on the other ranks): a step waits for its slowest rank."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -168,7 +170,8 @@ class ClockSampler:
             pass
 
     def __init__(self, device_index: int, period: float = 0.005, enabled: bool = True):
-        self.samples: list[tuple[int, int]] = []
+        self.samples: list[tuple[int, int]] = []  # taken while the GPU runs the timed steps
+        self.edge_samples: list[tuple[int, int]] = []  # just before and just after
         self.max_mhz = None
         self.period = period
         self._stop = threading.Event()
@@ -178,23 +181,32 @@ class ClockSampler:
         self._nvml = ClockSampler._nvml
         self._h, self.max_mhz = ClockSampler._handles[device_index]
 
-    def _sample(self):
+    def _sample(self, edge: bool = False):
         n = self._nvml
         mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
         reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-        self.samples.append((mhz, reasons))
+        (self.edge_samples if edge else self.samples).append((mhz, reasons))
 
     def _run(self):
+        self._go.wait()
         while not self._stop.is_set():
             try:
                 self._sample()
             except Exception:
                 return
-            time.sleep(self.period)
+            self._stop.wait(self.period)
+
+    def launched(self):
+        """The host has enqueued the timed steps: poll from now on, while the GPU works through
+        them. No poll overlaps the burst of launches (a poll that did stalled the multi-GPU step
+        by ~15 us per step over 200 steps at 2 GPUs)."""
+        if self._nvml:
+            self._go.set()
 
     def __enter__(self):
         if self._nvml:
-            self._sample()
+            self._sample(edge=True)  # before the region
+            self._go = threading.Event()
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
@@ -202,21 +214,26 @@ class ClockSampler:
     def __exit__(self, *exc):
         if self._nvml:
             self._stop.set()
+            self._go.set()
             self._t.join()
-            self._sample()
+            self._sample(edge=True)  # after the region
 
     def summary(self) -> dict | None:
-        if not self._nvml or not self.samples:
+        """Median SM clock and the union of clock-event reasons of the polls taken while the GPU ran
+        the timed steps (the two edge polls only if the region was too short for any)."""
+        used = self.samples or self.edge_samples
+        if not self._nvml or not used:
             return None
         reasons = 0
-        for _, r in self.samples:
+        for _, r in used:
             reasons |= r
         names = sorted(k for k, bit in self.REASONS.items() if reasons & bit and k != "gpu_idle")
         return {
-            "sm_mhz": statistics.median(m for m, _ in self.samples),
+            "sm_mhz": statistics.median(m for m, _ in used),
             "sm_max_mhz": self.max_mhz,
             "reasons": names,
-            "samples": len(self.samples),
+            "samples": len(used),
+            "in_region": bool(self.samples),
         }
 
 
@@ -332,8 +349,9 @@ def load_traffic(key: str) -> float | None:
         return None
 
 
-def time_back_to_back(fn, steps: int, stream) -> float:
-    """Milliseconds per call of `steps` back-to-back calls, CUDA events on the launching stream."""
+def time_back_to_back(fn, steps: int, stream, launched=None) -> float:
+    """Milliseconds per call of `steps` back-to-back calls, CUDA events on the launching stream
+    (`launched`, if given, is called once every call is enqueued)."""
     import torch
 
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -342,6 +360,8 @@ def time_back_to_back(fn, steps: int, stream) -> float:
     for i in range(steps):
         fn(i)
     b.record(stream)
+    if launched is not None:
+        launched()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / steps
 
@@ -652,7 +672,7 @@ def main() -> None:
             for _ in range(warmup):
                 one()
             with ClockSampler(torch.cuda.current_device()) as clocks:
-                ms = time_back_to_back(one, steps, stream)
+                ms = time_back_to_back(one, steps, stream, clocks.launched)
             clock_samples.append(clocks)
             step_ms += ms
             gbs = lay["work"].bytes / (ms * 1e-3) / 1e9
@@ -706,6 +726,7 @@ def main() -> None:
             for i in range(steps):
                 step(i)
             t1.record(stream)
+            clocks.launched()
             torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
