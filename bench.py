@@ -141,9 +141,9 @@ class ClockSampler:
     an `nvidia-smi` process polling alongside slowed the 2-GPU step tenfold). One poll is taken
     before the region; the side thread starts polling only once the host has enqueued every timed
     step (`launched`), so the polls fall while the GPU works through the region and never meet
-    the launch burst. Polls taken that way measured free (2 GPUs: 176.6-176.9 us per step polled
-    every 20 ms against 175.4-178.8 us unpolled). Multi-GPU runs poll rank 0's GPU only, every
-    20 ms (`enabled` False on the other ranks): a step waits for its slowest rank."""
+    the launch burst. On one GPU such polls cost nothing measurable. On several they still stall
+    the synchronised step (2 GPUs: 174 us unpolled, 187-204 us with two polls in the region), so
+    multi-GPU runs poll rank 0's GPU only, every 20 ms, in a repeat of the timed steps."""
 
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -718,25 +718,38 @@ def main() -> None:
         # one launch of the hot path (the fused gather included at N > 1; the cascade's three
         # kernels excepted), so the region's two events give the kernel's average launch duration
         # (an event between back-to-back launches would add ~5 us of launch gap to every step).
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(torch.cuda.current_device(), period=0.005 if world == 1 else 0.02,
-                          enabled=rank == 0) as clocks:
-            torch.cuda.synchronize()
-            t0.record(stream)
-            for i in range(steps):
-                step(i)
-            t1.record(stream)
-            clocks.launched()
-            torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        step_ms = t0.elapsed_time(t1) / steps
-        tt = torch.tensor([step_ms], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        step_ms = tt.item()
+        # At N = 1 the clocks are polled inside the timed region. At N > 1 a poll stalls the
+        # polled GPU for milliseconds and every rank waits for it at the step's end (2 GPUs: 174 us
+        # per step unpolled, 187-204 us with two polls in the region), so the timed region runs
+        # unpolled and the same K steps run again straight after it, on every rank, with rank 0
+        # polling: the clock record of that repeat stands beside the number, with its own time.
+        def timed_steps(sampler_on: bool):
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(torch.cuda.current_device(), period=0.005 if world == 1 else 0.02,
+                              enabled=sampler_on and rank == 0) as sampler:
+                torch.cuda.synchronize()
+                t0.record(stream)
+                for i in range(steps):
+                    step(i)
+                t1.record(stream)
+                sampler.launched()
+                torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            ms = torch.tensor([t0.elapsed_time(t1) / steps], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            return ms.item(), sampler
+
+        step_ms, clocks = timed_steps(world == 1)
         kern_ms = step_ms
         clocks_summary = clocks.summary()
+        if world > 1:
+            repeat_ms, clocks = timed_steps(True)
+            clocks_summary = clocks.summary()
+            if clocks_summary is not None:
+                clocks_summary.update(window="the same K steps repeated right after the timed region",
+                                      repeat_us_per_step=round(repeat_ms * 1e3, 2))
 
         # ---- end to end through the public API: pinned host inputs in, result out, every step
         if spec["kind"] == "decode":
