@@ -79,10 +79,14 @@ def run(cmd: list[str], verbose: bool) -> None:
 def build_library(force: bool = False, verbose: bool = False) -> Path:
     nvcc = str(cuda_home() / "bin" / "nvcc")
     OBJ_DIR.mkdir(exist_ok=True)
-    # --split-compile: the device compilation of one file runs on every core (the decode file's
-    # kernel instantiations take minutes on one).
+    # --split-compile: the device compilation of one file runs in parallel (the decode file's
+    # kernel instantiations take minutes on one thread). The count is fixed, not "every core":
+    # how the device code is split changes the registers ptxas gives the decode kernels, and with
+    # it their spills (bf16 decode kernels, spill loads in total: 13.1 KB split 8 ways, 24.5 KB
+    # split over an 8-core machine's "0", 17.5 KB unsplit; the two-n-tile kernel 1,364 against
+    # 2,024 bytes, which took ragged MQA from 295 to 409 us). Eight ways is the best measured.
     flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}",
-             "--split-compile=0"]
+             "--split-compile=8"]
     objs = []
     jobs = []
     for src in CU_SOURCES:

@@ -1492,13 +1492,17 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
       }
       named_barrier(1 + mu, TW * 32);
       if (tw == 0) {
+        // The combine slot of warp (ht, hg, t2 >= 1) is its warp index less HT * HG, i.e.
+        // (hg * HT + ht) + HT * HG * (t2 - 1): the (head, group) order of the warp index, which is
+        // not mu's (ht * HG + hg) when a tile has two or more heads and two or more groups.
+        const int wl = warp % (HT * HG);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int hl = nt * 8 + 2 * t4 + e;
             float M = m_run[nt][e];
-            for (int t2 = 1; t2 < TW; ++t2) M = fmaxf(M, red_m[(mu + HT * HG * (t2 - 1)) * HPW + hl]);
+            for (int t2 = 1; t2 < TW; ++t2) M = fmaxf(M, red_m[(wl + HT * HG * (t2 - 1)) * HPW + hl]);
             if (M == -INFINITY) continue;
             const float f0 = fast_exp2(m_run[nt][e] - M);
             float l = l_run[nt][e] * f0;
@@ -1508,7 +1512,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
               acc[mt][nt][2 + e] *= f0;
             }
             for (int t2 = 1; t2 < TW; ++t2) {
-              const int w2 = mu + HT * HG * (t2 - 1);  // combine slot of warp (ht, hg, t2)
+              const int w2 = wl + HT * HG * (t2 - 1);  // combine slot of warp (ht, hg, t2)
               const float m2 = red_m[w2 * HPW + hl];
               if (m2 == -INFINITY) continue;
               const float f = fast_exp2(m2 - M);
@@ -2497,10 +2501,11 @@ constexpr int kMaxStages = 24;
 // 256 x 512 and the 70B shape within 1 us of the cost-2 plan.
 constexpr int kTcSegmentCost = 4;
 
-// Optional tuning overrides read once from the environment:
+// Optional tuning overrides read from the environment on each call:
 //   KL_DECODE_HEADS_PER_TILE (1/2/4/8), KL_DECODE_STAGES (2..24), KL_DECODE_SEGMENT_COST
 //   (tiles charged per (sequence, unit) start by the balanced plan; negative: none),
-//   KL_DECODE_MIN_TILES (fewest tiles a CTA of the balanced plan takes). 0 = automatic.
+//   KL_DECODE_MIN_TILES (fewest tiles a CTA of the balanced plan takes), KL_DECODE_NT (1/2:
+//   8 or 16 query heads per warp, where the group allows). 0 = automatic.
 int env_int(const char* name) {
   const char* v = std::getenv(name);
   return v ? std::atoi(v) : 0;
@@ -2544,6 +2549,10 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
 
   p.D = D;
   int NT = (G > 8 && D <= 128) ? 2 : 1;
+  // KL_DECODE_NT=1 / 2 forces the query columns per warp (8 or 16 heads) where the shape allows.
+  const int forced_nt = env_int("KL_DECODE_NT");
+  if (forced_nt == 1 && (G + 7) / 8 <= kMaxHeadGroups) NT = 1;
+  if (forced_nt == 2 && D <= 128) NT = 2;
   // A cascade may widen the warps' query columns so that a prefix item packs more sequences
   // (KL_DECODE_CASCADE_NT=2; head_dim <= 128).
   if (cascade && env_int("KL_DECODE_CASCADE_NT") == 2 && D <= 128) NT = 2;

@@ -151,6 +151,30 @@ def test_head_layouts(hq, hkv, head_dim, dtype):
     assert_close_to_oracle(run_capi(q, kv), oracle_out(q, kv), dtype)
 
 
+@pytest.mark.parametrize(
+    "hq,hkv,head_dim,nt",
+    [
+        (48, 2, 128, "0"),  # default kernels: two KV heads a tile, two query groups a head, two
+        (64, 2, 128, "0"),  # warps splitting each (head, group)'s tiles
+        (32, 2, 256, "0"),
+        (32, 2, 128, "1"),  # the one-n-tile kernel forced (KL_DECODE_NT=1) on groups of 16 and 12
+        (24, 2, 128, "1"),
+        (64, 4, 128, "1"),  # four heads a tile, two groups, no split warps
+    ],
+)
+def test_tiles_of_several_heads_and_query_groups(hq, hkv, head_dim, nt, monkeypatch):
+    """Enough tiles that a tile holds two or more KV heads and each head's query heads span two
+    warp groups. The warps that split a (head, group)'s tiles combine through shared memory, and
+    the combine must find each partner warp's slot in the warp-index order: a mix-up of (head,
+    group) orders there only shows when both counts exceed one."""
+    from kernel_lab.kv_cache import random_decode_problem
+
+    monkeypatch.setenv("KL_DECODE_NT", nt)
+    q, kv, _, _ = random_decode_problem([1024] * 16 + [3000, 17], hq, hkv, head_dim, 16, dtype=torch.bfloat16,
+                                        device="cuda")
+    assert_close_to_oracle(run_capi(q, kv), oracle_out(q, kv), torch.bfloat16)
+
+
 @pytest.mark.parametrize("page_size", [1, 4, 8, 16, 32, 64, 128])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_page_sizes(page_size, dtype):
