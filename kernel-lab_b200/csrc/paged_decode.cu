@@ -2549,6 +2549,17 @@ int make_plan(int dtype, int batch, int Hq, int Hkv, int D, int P, int max_pages
 
   p.D = D;
   int NT = (G > 8 && D <= 128) ? 2 : 1;
+  // Groups of 9-32 query heads on small problems: 8 heads per warp (up to 4 warp groups a KV
+  // head) rather than 16. Each warp's tile work is shorter, which is what a problem of few tiles
+  // per SM is bound by. Measured at head_dim 128, bf16 (us, 16 against 8 heads a warp): MQA 32/1
+  // 4 x 4096 48.5 / 31.7, 8 x 4096 41.4 / 27.3, 32 x 4096 46.2 / 41.5 (55 tiles per SM),
+  // 1 x 32768 141.4 / 91.4; 32/2 16 x 4096 41.2 / 32.8; 64/4 8 x 4096 44.1 / 35.4. From about 110
+  // tiles per SM on, 16 heads a warp is faster (MQA 64 x 4096 58.5 / 62.9, 64/4 64 x 4096
+  // 105.6 / 125.1, config 4's ragged MQA 294 / 424). The table width stands in for the lengths.
+  if (NT == 2 && !cascade && !kv8 && D == 128 && (G + 7) / 8 <= kMaxHeadGroups &&
+      static_cast<int64_t>(batch) * max_tiles * Hkv < 64LL * sms) {
+    NT = 1;
+  }
   // KL_DECODE_NT=1 / 2 forces the query columns per warp (8 or 16 heads) where the shape allows.
   const int forced_nt = env_int("KL_DECODE_NT");
   if (forced_nt == 1 && (G + 7) / 8 <= kMaxHeadGroups) NT = 1;

@@ -154,11 +154,11 @@ def test_head_layouts(hq, hkv, head_dim, dtype):
 @pytest.mark.parametrize(
     "hq,hkv,head_dim,nt",
     [
-        (48, 2, 128, "0"),  # default kernels: two KV heads a tile, two query groups a head, two
-        (64, 2, 128, "0"),  # warps splitting each (head, group)'s tiles
-        (32, 2, 256, "0"),
-        (32, 2, 128, "1"),  # the one-n-tile kernel forced (KL_DECODE_NT=1) on groups of 16 and 12
-        (24, 2, 128, "1"),
+        (48, 2, 128, "2"),  # 16 query heads a warp (KL_DECODE_NT=2): two KV heads a tile, two
+        (64, 2, 128, "2"),  # query groups a head, two warps splitting each (head, group)'s tiles
+        (32, 2, 256, "0"),  # head_dim 256: 8 heads a warp, the same tile shape
+        (32, 2, 128, "1"),  # 8 query heads a warp (the default at this size) on groups of 16 and 12
+        (24, 2, 128, "0"),
         (64, 4, 128, "1"),  # four heads a tile, two groups, no split warps
     ],
 )
