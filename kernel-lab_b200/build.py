@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import argparse
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -68,35 +69,68 @@ def stale(target: Path, sources: list[Path]) -> bool:
     return any(s.stat().st_mtime > t for s in sources)
 
 
-def run(cmd: list[str], verbose: bool) -> None:
+def run(cmd: list[str], verbose: bool, cwd: Path | None = None) -> str:
     if verbose:
         print(" ".join(cmd), flush=True)
-    proc = subprocess.run(cmd, capture_output=True, text=True)
+    proc = subprocess.run(cmd, capture_output=True, text=True, cwd=cwd)
     if proc.returncode != 0:
         raise RuntimeError(f"build step failed ({proc.returncode}): {' '.join(cmd)}\n{proc.stdout}\n{proc.stderr}")
+    return proc.stderr
+
+
+def decode_spills(ptxas_log: str) -> dict[str, int]:
+    """Spill-load bytes per decode_tc_kernel instantiation, from ptxas's -v report."""
+    spills, kernel = {}, None
+    for line in ptxas_log.splitlines():
+        m = re.search(r"Compiling entry function '(\S+)'", line)
+        if m:
+            kernel = m.group(1)
+        m = re.search(r"(\d+) bytes spill loads", line)
+        if m and kernel and "decode_tc_kernel" in kernel:
+            spills[kernel] = int(m.group(1))
+    return spills
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
     nvcc = str(cuda_home() / "bin" / "nvcc")
     OBJ_DIR.mkdir(exist_ok=True)
-    # --split-compile: the device compilation of one file runs in parallel (the decode file's
-    # kernel instantiations take minutes on one thread). The count is fixed, not "every core":
-    # how the device code is split changes the registers ptxas gives the decode kernels, and with
-    # it their spills (bf16 decode kernels, spill loads in total: 13.1 KB split 8 ways, 24.5 KB
-    # split over an 8-core machine's "0", 17.5 KB unsplit; the two-n-tile kernel 1,364 against
-    # 2,024 bytes, which took ragged MQA from 295 to 409 us). Eight ways is the best measured.
-    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", f"-I{CSRC}",
-             "--split-compile=8"]
+    # The decode kernels run at their register cap (168 a thread), where ptxas's allocation tips on
+    # details of its input that have nothing to do with the code: the same source gave the headline
+    # kernel 0 or 212 bytes of spill loads and the two-n-tile kernel 1,364 or 2,024 (ragged MQA 295
+    # or 409 us) depending on the object file's path, the source path as given to nvcc, -lineinfo
+    # and the --split-compile partition count ("0" follows the machine's cores). For one input the
+    # result is the same every time. So nvcc runs from the repository root on relative paths,
+    # without -lineinfo, with 8 partitions; ptxas's report (-Xptxas -v) is read back, and the decode
+    # file is compiled under up to six trial object names, keeping the first whose one-n-tile
+    # kernels do not spill (else the fewest spills). The build prints which one it kept.
+    rel_include, rel_csrc = INCLUDE.relative_to(REPO), CSRC.relative_to(REPO)
+    base = [*ARCH, "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f"-I{rel_include}", f"-I{rel_csrc}", "-Xptxas", "-v"]
     objs = []
-    jobs = []
     for src in CU_SOURCES:
         obj = OBJ_DIR / (Path(src).stem + ".o")
         objs.append(obj)
-        if force or stale(obj, [CSRC / src, *HEADERS]):
-            jobs.append([nvcc, *flags, "-c", str(CSRC / src), "-o", str(obj)])
-    with ThreadPoolExecutor(max_workers=len(CU_SOURCES)) as pool:
-        list(pool.map(lambda c: run(c, verbose), jobs))
-    if force or jobs or stale(LIB, objs):
+        if not (force or stale(obj, [CSRC / src, *HEADERS])):
+            continue
+        rel_src = str(rel_csrc / src)
+        if src != "paged_decode.cu":
+            run([nvcc, *base, "--split-compile=8", "-c", rel_src, "-o", str(obj)], verbose, cwd=REPO)
+            continue
+        best = None
+        for k in range(6):
+            trial = OBJ_DIR / f"paged_decode.trial{k}.o"
+            spills = decode_spills(run([nvcc, *base, "--split-compile=8", "-c", rel_src, "-o", str(trial)],
+                                       verbose, cwd=REPO))
+            hot = sum(v for name, v in spills.items() if re.search(r"Li(64|128)ELi1E", name))
+            key = (hot, sum(spills.values()))
+            print(f"decode kernels, trial {k}: {key[1]} bytes of spill loads over {len(spills)} instantiations, "
+                  f"{hot} in the one-n-tile kernels", flush=True)
+            if best is None or key < best[0]:
+                best = (key, trial, k)
+            if hot == 0:
+                break
+        print(f"decode kernels: kept trial {best[2]}", flush=True)
+        shutil.copyfile(best[1], obj)
+    if force or stale(LIB, objs):
         run([nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs)], verbose)
     return LIB
 

@@ -218,7 +218,7 @@ __device__ __forceinline__ int clamp_prefix_len(const DecodeArgs& a, int p, bool
 // of the block; returns the total. Each thread scans a contiguous range, then one warp scans the
 // warps' sums. scratch: 33 ints. Ends with a block barrier.
 template <typename F>
-__device__ int block_scan(int n, F f, int* out, int* scratch) {
+__device__ __forceinline__ int block_scan(int n, F f, int* out, int* scratch) {
   const int nt = blockDim.x, tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
   const int per = (n + nt - 1) / nt;
@@ -274,7 +274,9 @@ __device__ __forceinline__ int group_of_entry(const int* vstart, int P, int e) {
 // table that is not a partition of the batch (indptr[0] = 0, non-decreasing, indptr[P] = batch)
 // turns the prefixes off and sets KL_STATUS_BAD_PREFIX_GROUPS. Ends with a block barrier.
 // `streams`: ranges per CTA (the plan is cut into gridDim.x * streams ranges).
-__device__ void plan_build(const DecodeArgs& a, const PlanSmem& ps, int streams = 1) {
+// The kernels' helpers are all force-inlined: the decode kernels run at their register cap, where a
+// helper compiled as a real call (with a stack frame) costs spills.
+__device__ __forceinline__ void plan_build(const DecodeArgs& a, const PlanSmem& ps, int streams = 1) {
   const int B = a.batch;
   const int nt = blockDim.x, tid = threadIdx.x;
   const bool report = blockIdx.x == 0;
@@ -791,7 +793,7 @@ __device__ __forceinline__ void cascade_arrive(const DecodeArgs& a, const RowSin
 // counts: a peer may already be one launch ahead), for at most g.wait_ns; on timeout it sets
 // kStatusPeerTimeout and leaves. It returns the count to zero for the next launch. One system-scope
 // fence per launch instead of one per thread: measured 176 against 188 us at two GPUs.
-__device__ void gather_finish(const DecodeArgs& a, int nthreads) {
+__device__ __forceinline__ void gather_finish(const DecodeArgs& a, int nthreads) {
   named_barrier(15, nthreads);
   if (threadIdx.x != 0) return;
   const Gather& g = a.gat;
@@ -824,7 +826,7 @@ __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return
 
 // groups > 0: a cascade over that many prefix groups (plan entries for prefix items as well).
 // streams > 1: each warp walks its own range (no combine slots).
-__host__ __device__ inline TcLayout tc_layout(int D, int NT, int TW, int streams, int nstage, int batch, int eb = 2,
+__host__ __device__ __forceinline__ TcLayout tc_layout(int D, int NT, int TW, int streams, int nstage, int batch, int eb = 2,
                                               int groups = 0, int HT = 1) {
   TcLayout L{};
   L.head_bytes = kTile * D * eb;  // one head's K (or V) rows of a tile (eb bytes per element)
@@ -926,8 +928,7 @@ __global__ void __launch_bounds__(kTCThreads, 1) decode_tc_kernel(const __grid_c
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int HT = cfg.ht, HG = cfg.hg, TW = cfg.tw, nstage = cfg.nstage;
-  // Streams exist only in the one-n-tile kernels; the others see the constant 1 (a runtime value
-  // there raised the two-n-tile kernel's spills from 1,364 to 2,024 bytes).
+  // Streams exist only in the one-n-tile kernels; the others see the constant 1.
   const int NS = NT == 1 ? cfg.ns : 1;  // streams (ranges) of this CTA
   const TcLayout L = tc_layout(D, NT, TW, NS, nstage, a.batch, EB, a.num_prefixes, HT);
   const uint32_t ring = smem_u32(smem + L.ring);
@@ -1742,7 +1743,7 @@ struct PrefixLayout {
 // Q [NH][128 rows x 128 B]; stage s: K and V [NH][128 tokens x 128 B]. P (128 rows x 128 tokens)
 // overwrites its stage's K once S has been computed when it fits (head_dim 128), otherwise it
 // has its own buffer per stage.
-__host__ __device__ inline PrefixLayout prefix_layout(int D) {
+__host__ __device__ __forceinline__ PrefixLayout prefix_layout(int D) {
   constexpr uint32_t CT = kPrefixTokens;
   const uint32_t nh = D / 64;
   const uint32_t kv = nh * CT * 128u;
@@ -2204,7 +2205,7 @@ struct GenLayout {
   uint32_t q, acc, p, m, l, alpha, rows, misc, prefix, lens, total;
 };
 
-__host__ __device__ inline GenLayout gen_layout(int G, int D, int batch) {
+__host__ __device__ __forceinline__ GenLayout gen_layout(int G, int D, int batch) {
   GenLayout L{};
   uint32_t off = 0;
   L.q = off;
