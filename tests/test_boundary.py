@@ -194,3 +194,51 @@ def test_extensions_share_the_process_libstdcxx():
         nm = subprocess.run(["nm", "-C", "--defined-only", str(so)], capture_output=True, text=True, check=True)
         bad = re.findall(r" [TW] (std::(?:codecvt|basic_ostream|locale)\S*)", nm.stdout)
         assert not bad, f"{so.name} defines libstdc++ internals: {bad[:3]}"
+
+
+def test_head_gather_descriptor_layout_matches_the_header(tmp_path):
+    """capi.HeadGather mirrors kl_head_gather_t: the size and every field's offset, as a C compiler
+    lays the header's struct out (gcc on the header itself), so a caller's descriptor is read
+    field for field by the library."""
+    import shutil
+
+    from kernel_lab import capi
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    fields = ["num_ranks", "rank", "epoch", "out", "flags", "done", "timeout_ms"]
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stddef.h>\n#include <stdio.h>\n#include "kernel_lab_b200.h"\nint main(void) {\n'
+        '  printf("%zu", sizeof(kl_head_gather_t));\n'
+        + "".join(f'  printf(" %zu", offsetof(kl_head_gather_t, {f}));\n' for f in fields)
+        + "  return 0;\n}\n"
+    )
+    exe = tmp_path / "layout"
+    cuda_inc = "/usr/local/cuda/include"
+    subprocess.run(["gcc", f"-I{REPO / 'include'}", f"-I{cuda_inc}", str(src), "-o", str(exe)], check=True)
+    c_size, *c_offsets = map(int, subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split())
+    assert ctypes.sizeof(capi.HeadGather) == c_size
+    assert [getattr(capi.HeadGather, f).offset for f in fields] == c_offsets
+
+
+def test_build_reads_decode_spills_from_the_ptxas_report():
+    """The build keeps the decode kernels' spill-free compilation by reading ptxas's -v report."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("kl_build", REPO / "kernel-lab_b200" / "build.py")
+    build = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(build)
+    log = (
+        "ptxas info    : Compiling entry function '_ZN3klb16decode_tc_kernelI13__nv_bfloat16Li128ELi1E' for 'sm_100a'\n"
+        "ptxas info    : Function properties for _ZN3klb16decode_tc_kernelI13__nv_bfloat16Li128ELi1E\n"
+        "    0 bytes stack frame, 0 bytes spill stores, 0 bytes spill loads\n"
+        "ptxas info    : Compiling entry function '_ZN3klb16decode_tc_kernelI6__halfLi128ELi2E' for 'sm_100a'\n"
+        "    232 bytes stack frame, 852 bytes spill stores, 1364 bytes spill loads\n"
+        "ptxas info    : Compiling entry function '_ZN3klb21rmsnorm_row_regs' for 'sm_100a'\n"
+        "    0 bytes stack frame, 8 bytes spill stores, 8 bytes spill loads\n"
+    )
+    assert build.decode_spills(log) == {
+        "_ZN3klb16decode_tc_kernelI13__nv_bfloat16Li128ELi1E": 0,
+        "_ZN3klb16decode_tc_kernelI6__halfLi128ELi2E": 1364,
+    }
